@@ -1,0 +1,447 @@
+"""Benchmark of the gated delta-rule hot path (driver contract: one JSON line).
+
+Headline workload (BASELINE configs[1] at its largest batch, which is also
+config 4 at N=1): GDN decode, B=1024, Hqk=16, Hv=32, d_k=d_v=128, fp32 state
+(4.3 GB of algorithmic traffic per step: larger than L2, so no flush is
+needed), one decode token per step, state updated in place.  With N GPUs the
+32 value heads are sharded Hv/N per GPU (fixed total work: strong scaling)
+and the outputs are all-gathered over NVLink (NCCL) once per step.
+
+  value : algorithmic state GB/s of the whole job, device-timed (CUDA events,
+          max over ranks), inputs resident in HBM.
+  e2e   : the same metric through the public API with host buffers: every step
+          copies its q/k/v/g/beta from pinned host memory, launches, and reads
+          o back to pinned host memory inside the timed region.
+``--impl reference`` times the reference's CPU recurrence (the oracle port,
+all host threads) on the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import __graft_entry__ as graft  # noqa: E402
+
+METRIC = "GDN decode state GB/s"
+UNIT = "GB/s"
+B, HQK, HV, D = 1024, 16, 32, 128
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return j["hbm_gbs"], j.get("bf16_tflops", BF16_FALLBACK_TFLOPS), "measured"
+    return HBM_FALLBACK_GBS, BF16_FALLBACK_TFLOPS, "fallback"
+
+
+def profiled_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<name>.md,
+    line 'traffic_bytes_per_launch: N'), or None."""
+    f = ROOT / "profiles" / f"{name}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return int(float(line.split(":", 1)[1]))
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.25)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------- CPU
+def cpu_sample(seconds: float = 10.0):
+    """The oracle port (C, all host threads) on a bounded sample of the
+    headline workload: batches of 32 sequences x 32 value heads, one decode
+    step each, repeated for about `seconds`.  Returns (GB/s, threads, text)."""
+    orc = graft.oracle()
+    inputs = graft.submodule("inputs")
+    Bs = 32
+    x = inputs.make_decode_inputs(1, Bs, HQK, HV, D, seed=0)
+    args = [t.float().numpy() for t in (x.q, x.k, x.v, x.g, x.beta)]
+    S = x.state.numpy()
+    orc.gdn_decode_steps(*args, S)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        orc.gdn_decode_steps(*args, S)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = n * graft.submodule("inputs").gdn_decode_bytes(Bs, HQK, HV, D, D) / el / 1e9
+    sample = (f"{n} one-step calls of B={Bs} (of {B}) x Hv={HV} heads, d=128, "
+              f"{el:.1f} s of CPU work")
+    return gbs, orc.num_threads(), sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    inputs = graft.submodule("inputs")
+    orc = graft.oracle()
+    Bs = 32
+    x = inputs.make_decode_inputs(1, Bs, HQK, HV, D, seed=0)
+    a = [t.float().numpy() for t in (x.q, x.k, x.v, x.g, x.beta)]
+    S = x.state.numpy()
+    for _ in range(args.warmup):
+        orc.gdn_decode_steps(*a, S)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.gdn_decode_steps(*a, S)
+    el = time.perf_counter() - t0
+    gbs = args.steps * inputs.gdn_decode_bytes(Bs, HQK, HV, D, D) / el / 1e9
+    ms = el / args.steps * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (BASELINE distributions, seed 0)",
+        "config": {"workload": "GDN decode B=1024 Hqk=16 Hv=32 d=128 (CPU: bounded sample of "
+                               f"B={Bs} sequences per step)", "global_batch": B,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": orc.num_threads(),
+                         "kind": "port",
+                         "sample": f"each step: one decode step of B={Bs} x Hv={HV} heads "
+                                   "through the C restatement of gdn_decode_reference"},
+        "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU
+def run_gpu(args, world, rank, local):
+    pkg = graft.package()
+    inputs = graft.submodule("inputs")
+    sharded = graft.submodule("sharded")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shard = sharded.shard_heads(HV, HQK, world, rank)
+    hv, hq = shard.h1 - shard.h0, shard.hq1 - shard.hq0
+    pool = 4  # distinct token inputs cycled through the steps
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    state = torch.randn((B, hv, D, D), generator=gen, device=dev) * 0.02
+    toks = []
+    for i in range(pool):
+        x = inputs.make_decode_inputs(1, B, hq, hv, D, seed=100 * rank + i, device=dev,
+                                      state_std=0.0)
+        toks.append([x.q[0], x.k[0], x.v[0], x.g[0], x.beta[0]])
+    out = torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev)
+    steps = [pkg.DecodeStep(*t, state, out=out) for t in toks]
+    gather_buf = torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    def one_step(i):
+        steps[i % pool]()
+        if world > 1:
+            dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        one_step(i)
+    pkg.check_device_status(dev)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            kev[i][0].record(stream)
+            steps[i % pool]()
+            kev[i][1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    pkg.check_device_status(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
+    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps, world, dev)
+    total_bytes = inputs.gdn_decode_bytes(B, HQK, HV, D, D)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    local_bytes = inputs.gdn_decode_bytes(B, hq, hv, D, D)
+    hbm, bf16, peak_kind = peaks()
+    achieved = local_bytes / (kern_ms * 1e-3) / 1e9
+
+    # ---- e2e through the public API with pinned host buffers
+    e2e_steps = min(args.steps, 200)
+    host = [[t.cpu().pin_memory() for t in tk] for tk in toks]
+    dev_in = toks  # the bound device buffers the DecodeSteps read
+    o_host = torch.empty((B, HV if world > 1 else hv, D), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    d2h = o_host.numel() * o_host.element_size() if (world == 1 or rank == 0) else 0
+    full_o = torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    def e2e_step(i):
+        j = i % pool
+        for hsrc, ddst in zip(host[j], dev_in[j]):
+            ddst.copy_(hsrc, non_blocking=True)
+        steps[j]()
+        if world > 1:
+            dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
+            full_o.view(B, world, hv, D).copy_(gather_buf.permute(1, 0, 2, 3))
+            if rank == 0:
+                o_host.copy_(full_o, non_blocking=True)
+        else:
+            o_host.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world, dev)
+    e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
+
+    extras = {}
+    cpu = None
+    if world == 1 and not args.no_extras:
+        extras = run_extras(pkg, inputs, dev, hbm, bf16)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, cores, sample = cpu_sample(args.cpu_seconds)
+        cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": sample}
+    if rank != 0:
+        return
+    traffic = profiled_traffic("gdn_decode_B1024")
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (BASELINE distributions, seed 0)",
+        "config": {"workload": "GDN decode (BASELINE configs[1], B=1024; config 4 at N>1)",
+                   "global_batch": B, "Hqk": HQK, "Hv": HV, "d_k": D, "d_v": D,
+                   "io_dtype": "bf16", "state": "fp32 in place",
+                   "parallelism": f"value-head shard x{world}" + (" + NCCL all-gather of o"
+                                                                 if world > 1 else ""),
+                   "l2": "inputs larger than L2 (4.3 GB state), no flush"},
+        "tokens_per_s": round(B / (ms * 1e-3), 1),
+        "pct_of_8TBs": round(100 * value / 8000.0, 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "peak_kind": f"{peak_kind} (burst copy)",
+                     "kernel": "decode_kernel<128,128,bf16,GDN>",
+                     "algorithmic_bytes_per_launch": local_bytes},
+        "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+        "extras": extras,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _time_graph(fn, reps=20, warm=3):
+    """Captures fn() in a CUDA graph and returns ms per replay."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    for _ in range(warm):
+        g.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_extras(pkg, inputs, dev, hbm, bf16):
+    """Secondary BASELINE configs, device-timed (not the headline)."""
+    ex = {}
+    # config 0: B=8, 64 sequential steps per CUDA-graph replay
+    x = inputs.make_decode_inputs(64, 8, HQK, HV, D, seed=0, device=dev)
+    st = x.state.clone()
+    o = torch.empty((8, HV, D), dtype=torch.bfloat16, device=dev)
+    s0 = [pkg.DecodeStep(x.q[t], x.k[t], x.v[t], x.g[t], x.beta[t], st, out=o) for t in range(64)]
+    ms = _time_graph(lambda: [s() for s in s0])
+    ex["config0_gdn_B8_64steps"] = {
+        "tokens_per_s": round(8 * 64 / (ms * 1e-3), 1), "us_per_step": round(ms * 1e3 / 64, 3),
+        "state_GBps_equiv": round(64 * inputs.gdn_decode_bytes(8, HQK, HV) / (ms * 1e-3) / 1e9, 1),
+        "note": "16.8 MB state is L2-resident; GB/s-equivalent can exceed HBM peak"}
+    del x, st, s0
+    # config 1 sweep (B=64, 256): one step per replay, state in place
+    for b in (64, 256):
+        x = inputs.make_decode_inputs(1, b, HQK, HV, D, seed=1, device=dev)
+        st = x.state.clone()
+        s1 = pkg.DecodeStep(x.q[0], x.k[0], x.v[0], x.g[0], x.beta[0], st)
+        ms = _time_graph(lambda: s1(), reps=100)
+        gbs = inputs.gdn_decode_bytes(b, HQK, HV) / (ms * 1e-3) / 1e9
+        ex[f"config1_gdn_B{b}"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                                   "us": round(ms * 1e3, 2)}
+        del x, st, s1
+    # config 2: KDA B=64, H=32, 64 steps per replay
+    x = inputs.make_decode_inputs(64, 64, 32, 32, D, kda=True, seed=2, device=dev)
+    st = x.state.clone()
+    o = torch.empty((64, 32, D), dtype=torch.bfloat16, device=dev)
+    s2 = [pkg.DecodeStep(x.q[t], x.k[t], x.v[t], x.g[t], x.beta[t], st, out=o, kda=True)
+          for t in range(64)]
+    ms = _time_graph(lambda: [s() for s in s2], reps=10)
+    gbs = 64 * inputs.kda_decode_bytes(64, 32, 32) / (ms * 1e-3) / 1e9
+    ex["config2_kda_B64_64steps"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                                     "us_per_step": round(ms * 1e3 / 64, 2),
+                                     "note": "268 MB state; partly L2-resident across steps"}
+    del x, st, s2
+    # config 3: chunked prefill
+    try:
+        p = inputs.make_prefill_inputs(4, 4096, HQK, HV, D, seed=3, device=dev)
+        fs = torch.empty((4, HV, D, D), dtype=torch.float32, device=dev)
+        po = torch.empty((4, 4096, HV, D), dtype=torch.bfloat16, device=dev)
+        fn = lambda: pkg.gdn_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(10):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 10
+        fl = inputs.gdn_prefill_flops(4, 4096, HQK, HV, D, 64)
+        tf = fl / (ms * 1e-3) / 1e12
+        ex["config3_prefill_B4_T4096"] = {"ms": round(ms, 4), "TFLOPs": round(tf, 1),
+                                          "frac_of_bf16_peak": round(tf / bf16, 4),
+                                          "chunked_form_GFLOP": round(fl / 1e9, 2)}
+    except Exception as e:  # prefill not available yet
+        ex["config3_prefill_B4_T4096"] = {"unavailable": str(e)[:200]}
+    return ex
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            graft.build()
+            run_gpu(args, world, rank, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

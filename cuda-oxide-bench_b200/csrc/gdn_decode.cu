@@ -1,0 +1,451 @@
+// gdn_decode.cu — GDN and KDA single-token decode for sm_100a.
+//
+// Math (per batch b, value head h; S is d_k x d_v fp32, row k, column v):
+//     S_s = a * S            a = exp(g) scalar (GDN) or exp(g[k]) per row (KDA)
+//     u   = k^T S_s          (one value per column)
+//     r   = v - u
+//     S'  = S_s + beta * k r^T
+//     o   = scale * S'^T q = scale * (q^T S_s + beta * (q.k) * r)
+// following gdn_decode_reference
+// (analysis/wave15-attention-architecture/reference/pytorch_reference_gdn.py:38-91)
+// and naive_recurrent_kda_step (pytorch_reference_kda.py:42-71).  The last
+// identity lets one pass over S produce both column reductions, so the state
+// crosses HBM exactly once in each direction.
+//
+// Work unit ("slab"): the DK x BV block of one head's state holding BV value
+// columns.  Columns are independent, so slabs need no communication.
+//
+// Kernel structure (persistent, one CTA per SM, 9 warps):
+//   warp 8 (producer): for each slab in the CTA's static schedule waits for a
+//     free ring slot, then stages the slab plus the q/k rows, the v slice and
+//     (KDA) the gate row into shared memory with cp.async.bulk, completing on
+//     the slot's "full" mbarrier.  A contiguous slab (BV == d_v) is a single
+//     bulk copy; otherwise one copy per state row.
+//   warps 0-7 (consumers): wait "full", pull their rows of the slab into
+//     registers with 16-byte shared loads, release the slot ("empty"), then
+//     reduce k.S, q.S and q.k across rows (warp shuffles, then a ping-pong
+//     shared buffer across warps), and write the updated rows straight back to
+//     the state with 16-byte global stores (in place when state_out ==
+//     state_in: each slab is read completely before any of it is written and
+//     slabs are disjoint).
+// Every mbarrier wait is bounded; a timeout sets a status bit and unwinds.
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace gdn {
+
+struct DecodeParams {
+  gdn_decode_args_t a;
+  int64_t total_slabs;
+  int32_t nvb;        // value-column blocks per head (d_v / BV)
+  int32_t group;      // Hv / Hqk
+  int32_t stages;     // ring depth
+  int32_t stage_bytes;
+  int32_t contiguous; // BV == d_v: a slab is one contiguous block
+  int32_t g_row_bytes;
+};
+
+template <int DK, int BV, bool KDA>
+struct DecodeTraits {
+  static constexpr int kConsumerWarps = 8;
+  static constexpr int kConsumers = kConsumerWarps * 32;
+  static constexpr int kThreads = kConsumers + 32;
+  static constexpr int kColGroups = BV / 4;                  // float4 columns
+  static constexpr int kRowGroups = kConsumers / kColGroups;  // thread rows
+  static constexpr int kRows = DK / kRowGroups;               // rows per thread
+  static constexpr int kMaxStages = 8;
+  static constexpr uint32_t kSlabBytes = DK * BV * 4;
+  static constexpr uint32_t kQKBytes = DK * 2;
+  static constexpr uint32_t kVBytes = BV * 2;
+  static constexpr uint32_t kGBytes = KDA ? DK * 4 : 0;  // room for an fp32 gate row
+  static constexpr uint32_t kStageBytes =
+      (kSlabBytes + 2 * kQKBytes + kVBytes + kGBytes + 127) / 128 * 128;
+  // header: 2*8 mbarriers + abort flag (256 B), then the reduction buffers
+  static constexpr uint32_t kRedFloats = 2 * kConsumerWarps * BV * 2 + 2 * kConsumerWarps;
+  static constexpr uint32_t kHeaderBytes = (256 + kRedFloats * 4 + 127) / 128 * 128;
+  static_assert(kColGroups <= 32 && 32 % kColGroups == 0, "BV must be 32..128");
+  static_assert(DK % kRowGroups == 0, "DK must be a multiple of the row groups");
+};
+
+template <int DK, int BV, typename IO, bool KDA>
+__global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
+    decode_kernel(const DecodeParams p) {
+  using Tr = DecodeTraits<DK, BV, KDA>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + Tr::kMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + Tr::kMaxStages);
+  float* red = reinterpret_cast<float*>(smem + 256);  // [2][warps][2][BV]
+  float* red_qk = red + 2 * Tr::kConsumerWarps * BV * 2;  // [2][warps]
+  unsigned char* ring = smem + Tr::kHeaderBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const gdn_decode_args_t& a = p.a;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], Tr::kConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == Tr::kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    int it = 0;
+    for (int64_t slab = blockIdx.x; slab < p.total_slabs; slab += gridDim.x, ++it) {
+      const int stage = it % p.stages;
+      const uint32_t round = it / p.stages;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(&empty[stage], (round & 1) ^ 1);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || *abort_flag) {
+        if (!ok && lane == 0) {
+          report(a.status, GDN_DEVERR_EMPTY_TIMEOUT);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      const int64_t bh = slab / p.nvb;
+      const int vb = static_cast<int>(slab - bh * p.nvb);
+      const int64_t b = bh / a.Hv;
+      const int h = static_cast<int>(bh - b * a.Hv);
+      const int hq = h / p.group;
+      unsigned char* st = ring + static_cast<size_t>(stage) * p.stage_bytes;
+      const float* src = a.state_in + (bh * DK) * a.dv + static_cast<int64_t>(vb) * BV;
+      if (lane == 0) {
+        uint32_t bytes = 2 * Tr::kQKBytes + Tr::kVBytes;
+        if (KDA) bytes += p.g_row_bytes;
+        if (p.contiguous) bytes += Tr::kSlabBytes;
+        mbar_expect_tx(&full[stage], bytes);
+        const IO* q = static_cast<const IO*>(a.q) + b * a.q_sb + static_cast<int64_t>(hq) * a.q_sh;
+        const IO* k = static_cast<const IO*>(a.k) + b * a.k_sb + static_cast<int64_t>(hq) * a.k_sh;
+        const IO* v = static_cast<const IO*>(a.v) + b * a.v_sb + static_cast<int64_t>(h) * a.v_sh +
+                      static_cast<int64_t>(vb) * BV;
+        bulk_g2s(st + Tr::kSlabBytes, q, Tr::kQKBytes, &full[stage]);
+        bulk_g2s(st + Tr::kSlabBytes + Tr::kQKBytes, k, Tr::kQKBytes, &full[stage]);
+        bulk_g2s(st + Tr::kSlabBytes + 2 * Tr::kQKBytes, v, Tr::kVBytes, &full[stage]);
+        if (KDA) {
+          const unsigned char* g = static_cast<const unsigned char*>(a.g) +
+                                   (b * a.g_sb + static_cast<int64_t>(h) * a.g_sh) *
+                                       (a.g_dtype == GDN_DT_F32 ? 4 : 2);
+          bulk_g2s(st + Tr::kSlabBytes + 2 * Tr::kQKBytes + Tr::kVBytes, g, p.g_row_bytes,
+                   &full[stage]);
+        }
+        if (p.contiguous) bulk_g2s(st, src, Tr::kSlabBytes, &full[stage]);
+      }
+      if (!p.contiguous) {
+        // one bulk copy per state row, spread over the warp's lanes
+        constexpr int kRowsPerLane = (DK + 31) / 32;
+        int mine = 0;
+        for (int r = lane; r < DK; r += 32) ++mine;
+        (void)kRowsPerLane;
+        if (mine) mbar_expect_tx(&full[stage], mine * BV * 4);
+        for (int r = lane; r < DK; r += 32)
+          bulk_g2s(st + r * BV * 4, src + static_cast<int64_t>(r) * a.dv, BV * 4, &full[stage]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[stage]);
+    }
+    // On abort, copies issued into slots the consumers never drained may still
+    // be in flight: wait (bounded) for them before the CTA's shared memory is
+    // released.
+    if (*abort_flag && lane == 0) {
+      const int n = it < p.stages ? it : p.stages;
+      for (int j = 0; j < n; ++j) {
+        const int jt = it - 1 - j;
+        if (jt < 0) break;
+        if (!mbar_wait_bounded(&full[jt % p.stages], (jt / p.stages) & 1)) {
+          report(a.status, GDN_DEVERR_DRAIN_TIMEOUT);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int tid = threadIdx.x;                 // 0 .. kConsumers-1
+  const int cg = tid % Tr::kColGroups;         // float4 column group
+  const int rg = tid / Tr::kColGroups;         // first row of this thread
+  const float scale = a.scale;
+  int it = 0;
+  for (int64_t slab = blockIdx.x; slab < p.total_slabs; slab += gridDim.x, ++it) {
+    const int stage = it % p.stages;
+    const uint32_t round = it / p.stages;
+    const int64_t bh = slab / p.nvb;
+    const int vb = static_cast<int>(slab - bh * p.nvb);
+    const int64_t b = bh / a.Hv;
+    const int h = static_cast<int>(bh - b * a.Hv);
+
+    // per-(b,h) scalars: issued before the wait so their latency overlaps it
+    const float beta = load_any(a.beta, b * a.beta_sb + static_cast<int64_t>(h) * a.beta_sh,
+                                a.beta_dtype);
+    float alpha = 1.f;
+    if (!KDA) {
+      const float g = load_any(a.g, b * a.g_sb + static_cast<int64_t>(h) * a.g_sh, a.g_dtype);
+      alpha = (a.gate_kind == GDN_GATE_LOG) ? __expf(g) : g;
+    }
+
+    // A timed-out thread still runs to the reduction barrier below, where the
+    // consumers agree (bar.red.or) to stop together; no thread is left behind
+    // on a barrier.
+    const bool landed = mbar_wait_bounded(&full[stage], round & 1);
+    const unsigned char* st = ring + static_cast<size_t>(stage) * p.stage_bytes;
+    const float* s_slab = reinterpret_cast<const float*>(st);
+    const IO* s_q = reinterpret_cast<const IO*>(st + Tr::kSlabBytes);
+    const IO* s_k = reinterpret_cast<const IO*>(st + Tr::kSlabBytes + Tr::kQKBytes);
+    const IO* s_v = reinterpret_cast<const IO*>(st + Tr::kSlabBytes + 2 * Tr::kQKBytes);
+    const void* s_g = st + Tr::kSlabBytes + 2 * Tr::kQKBytes + Tr::kVBytes;
+
+    float4 s[Tr::kRows];
+    float kr[Tr::kRows];
+    float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 qs = make_float4(0.f, 0.f, 0.f, 0.f);
+    float qk = 0.f;
+#pragma unroll
+    for (int i = 0; i < Tr::kRows; ++i) {
+      const int row = rg + i * Tr::kRowGroups;
+      float4 x = lds128(s_slab + row * BV + cg * 4);
+      const float kv = to_f32(s_k[row]);
+      const float qv = to_f32(s_q[row]);
+      float ai = alpha;
+      if (KDA) {
+        const float gr = smem_any(s_g, row, a.g_dtype);
+        ai = (a.gate_kind == GDN_GATE_LOG) ? __expf(gr) : gr;
+      }
+      x.x *= ai; x.y *= ai; x.z *= ai; x.w *= ai;
+      u.x = fmaf(kv, x.x, u.x); u.y = fmaf(kv, x.y, u.y);
+      u.z = fmaf(kv, x.z, u.z); u.w = fmaf(kv, x.w, u.w);
+      qs.x = fmaf(qv, x.x, qs.x); qs.y = fmaf(qv, x.y, qs.y);
+      qs.z = fmaf(qv, x.z, qs.z); qs.w = fmaf(qv, x.w, qs.w);
+      qk = fmaf(qv, kv, qk);
+      s[i] = x;
+      kr[i] = kv;
+    }
+    float4 vv;
+    vv.x = to_f32(s_v[cg * 4 + 0]);
+    vv.y = to_f32(s_v[cg * 4 + 1]);
+    vv.z = to_f32(s_v[cg * 4 + 2]);
+    vv.w = to_f32(s_v[cg * 4 + 3]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);  // slot may be refilled now
+
+    // reduce over the row groups inside this warp
+#pragma unroll
+    for (int off = Tr::kColGroups; off < 32; off <<= 1) {
+      u.x += __shfl_xor_sync(0xffffffffu, u.x, off);
+      u.y += __shfl_xor_sync(0xffffffffu, u.y, off);
+      u.z += __shfl_xor_sync(0xffffffffu, u.z, off);
+      u.w += __shfl_xor_sync(0xffffffffu, u.w, off);
+      qs.x += __shfl_xor_sync(0xffffffffu, qs.x, off);
+      qs.y += __shfl_xor_sync(0xffffffffu, qs.y, off);
+      qs.z += __shfl_xor_sync(0xffffffffu, qs.z, off);
+      qs.w += __shfl_xor_sync(0xffffffffu, qs.w, off);
+      qk += __shfl_xor_sync(0xffffffffu, qk, off);
+    }
+    // ... then across warps through a ping-pong buffer (one barrier per slab)
+    float* rb = red + (it & 1) * (Tr::kConsumerWarps * BV * 2);
+    float* rq = red_qk + (it & 1) * Tr::kConsumerWarps;
+    if (lane < Tr::kColGroups) {
+      *reinterpret_cast<float4*>(rb + warp * BV * 2 + cg * 4) = u;
+      *reinterpret_cast<float4*>(rb + warp * BV * 2 + BV + cg * 4) = qs;
+    }
+    if (lane == 0) rq[warp] = qk;
+    if (named_barrier_or(1, Tr::kConsumers, !landed)) {
+      if (!landed) report(a.status, GDN_DEVERR_FULL_TIMEOUT);
+      *abort_flag = 1;
+      break;
+    }
+    u = make_float4(0.f, 0.f, 0.f, 0.f);
+    qs = make_float4(0.f, 0.f, 0.f, 0.f);
+    qk = 0.f;
+#pragma unroll
+    for (int w = 0; w < Tr::kConsumerWarps; ++w) {
+      const float4 pu = *reinterpret_cast<const float4*>(rb + w * BV * 2 + cg * 4);
+      const float4 pq = *reinterpret_cast<const float4*>(rb + w * BV * 2 + BV + cg * 4);
+      u.x += pu.x; u.y += pu.y; u.z += pu.z; u.w += pu.w;
+      qs.x += pq.x; qs.y += pq.y; qs.z += pq.z; qs.w += pq.w;
+      qk += rq[w];
+    }
+    float4 r;
+    r.x = vv.x - u.x; r.y = vv.y - u.y; r.z = vv.z - u.z; r.w = vv.w - u.w;
+
+    if (rg == 0) {
+      const float bqk = beta * qk;
+      IO ov[4];
+      ov[0] = from_f32<IO>(scale * fmaf(bqk, r.x, qs.x));
+      ov[1] = from_f32<IO>(scale * fmaf(bqk, r.y, qs.y));
+      ov[2] = from_f32<IO>(scale * fmaf(bqk, r.z, qs.z));
+      ov[3] = from_f32<IO>(scale * fmaf(bqk, r.w, qs.w));
+      IO* o = static_cast<IO*>(a.o) + b * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
+              static_cast<int64_t>(vb) * BV + cg * 4;
+      *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(ov);
+    }
+
+    float* dst = a.state_out + (bh * DK) * a.dv + static_cast<int64_t>(vb) * BV + cg * 4;
+#pragma unroll
+    for (int i = 0; i < Tr::kRows; ++i) {
+      const int row = rg + i * Tr::kRowGroups;
+      const float bk = beta * kr[i];
+      float4 x = s[i];
+      x.x = fmaf(bk, r.x, x.x); x.y = fmaf(bk, r.y, x.y);
+      x.z = fmaf(bk, r.z, x.z); x.w = fmaf(bk, r.w, x.w);
+      stg128(dst + static_cast<int64_t>(row) * a.dv, x);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ launcher
+
+template <int DK, int BV, typename IO, bool KDA>
+static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
+  using Tr = DecodeTraits<DK, BV, KDA>;
+  static std::atomic<uint64_t> attr_done{0};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int stages = (di.smem_optin - static_cast<int>(Tr::kHeaderBytes)) / static_cast<int>(Tr::kStageBytes);
+  if (stages > Tr::kMaxStages) stages = Tr::kMaxStages;
+  if (stages < 2) return GDN_ERR_SHAPE;
+  const int smem = Tr::kHeaderBytes + stages * Tr::kStageBytes;
+  auto kern = decode_kernel<DK, BV, IO, KDA>;
+  rc = ensure_smem_attr(kern, smem, attr_done);
+  if (rc) return rc;
+
+  DecodeParams p;
+  p.a = a;
+  p.nvb = a.dv / BV;
+  p.total_slabs = static_cast<int64_t>(a.B) * a.Hv * p.nvb;
+  p.group = a.Hv / a.Hqk;
+  p.stages = stages;
+  p.stage_bytes = Tr::kStageBytes;
+  p.contiguous = (BV == a.dv) ? 1 : 0;
+  p.g_row_bytes = KDA ? DK * host_dtype_size(a.g_dtype) : 0;
+  const int64_t grid64 = p.total_slabs < di.sm_count ? p.total_slabs : di.sm_count;
+  kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+static int validate_decode(const gdn_decode_args_t* a, bool kda) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->state_in || !a->state_out || !a->o)
+    return GDN_ERR_NULL;
+  if (a->B < 1 || a->Hqk < 1 || a->Hv < 1 || a->Hv % a->Hqk) return GDN_ERR_SHAPE;
+  if (a->dk != 64 && a->dk != 128 && a->dk != 256) return GDN_ERR_SHAPE;
+  if (a->dv < 64 || a->dv % 64) return GDN_ERR_SHAPE;
+  if (a->io_dtype != GDN_DT_BF16 && a->io_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
+  if (!dtype_valid(a->g_dtype) || !dtype_valid(a->beta_dtype)) return GDN_ERR_DTYPE;
+  if (a->gate_kind != GDN_GATE_LOG && a->gate_kind != GDN_GATE_LINEAR) return GDN_ERR_DTYPE;
+  // bulk-copied rows: 16-byte aligned bases and strides
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) ||
+      !aligned16(a->state_in) || !aligned16(a->state_out))
+    return GDN_ERR_ALIGN;
+  if (!stride_ok(a->q_sb, 2) || !stride_ok(a->q_sh, 2) || !stride_ok(a->k_sb, 2) ||
+      !stride_ok(a->k_sh, 2) || !stride_ok(a->v_sb, 2) || !stride_ok(a->v_sh, 2) ||
+      !stride_ok(a->o_sb, 2) || !stride_ok(a->o_sh, 2))
+    return GDN_ERR_ALIGN;
+  if (kda) {
+    const int gs = host_dtype_size(a->g_dtype);
+    if (!aligned16(a->g) || !stride_ok(a->g_sb, gs) || !stride_ok(a->g_sh, gs)) return GDN_ERR_ALIGN;
+  }
+  // in place, or fully disjoint
+  if (a->state_in != a->state_out) {
+    const size_t n = static_cast<size_t>(a->B) * a->Hv * a->dk * a->dv;
+    const float* i0 = a->state_in;
+    const float* o0 = a->state_out;
+    if (i0 < o0 + n && o0 < i0 + n) return GDN_ERR_SHAPE;
+  }
+  return GDN_OK;
+}
+
+// Chooses the value-column block: whole rows when that still gives every SM
+// at least two slabs, otherwise 64-column blocks for better balance.
+static int pick_bv(const gdn_decode_args_t& a, int sm_count) {
+  if (a.dk <= 128 && a.dv % 128 == 0) {
+    const int64_t slabs128 = static_cast<int64_t>(a.B) * a.Hv * (a.dv / 128);
+    if (a.dk == 64 || slabs128 >= 2 * static_cast<int64_t>(sm_count)) return a.dk == 64 ? 64 : 128;
+  }
+  return 64;
+}
+
+template <typename IO, bool KDA>
+static int dispatch_dk(const gdn_decode_args_t& a, cudaStream_t stream, int bv) {
+  switch (a.dk) {
+    case 64: return launch_decode_impl<64, 64, IO, KDA>(a, stream);
+    case 128:
+      return bv == 128 ? launch_decode_impl<128, 128, IO, KDA>(a, stream)
+                       : launch_decode_impl<128, 64, IO, KDA>(a, stream);
+    case 256: return launch_decode_impl<256, 64, IO, KDA>(a, stream);
+  }
+  return GDN_ERR_SHAPE;
+}
+
+static int decode_entry(const gdn_decode_args_t* a, cudaStream_t stream, bool kda) {
+  int rc = validate_decode(a, kda);
+  if (rc) return rc;
+  DeviceInfo di;
+  rc = device_info(&di);
+  if (rc) return rc;
+  const int bv = pick_bv(*a, di.sm_count);
+  if (a->io_dtype == GDN_DT_BF16)
+    return kda ? dispatch_dk<__nv_bfloat16, true>(*a, stream, bv)
+               : dispatch_dk<__nv_bfloat16, false>(*a, stream, bv);
+  return kda ? dispatch_dk<__half, true>(*a, stream, bv) : dispatch_dk<__half, false>(*a, stream, bv);
+}
+
+}  // namespace gdn
+
+extern "C" int gdn_decode_launch(const gdn_decode_args_t* args, gdn_stream_t stream) {
+  return gdn::decode_entry(args, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int kda_decode_launch(const gdn_decode_args_t* args, gdn_stream_t stream) {
+  return gdn::decode_entry(args, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+static gdn_decode_args_t ref_layout_args(int32_t B, int32_t H, int32_t dk, int32_t dv,
+                                         const void* dQ, const void* dK, const void* dV,
+                                         const void* dG, const void* dBeta, const float* dS_in,
+                                         float* dS_out, void* dO, int32_t io_dtype, bool kda) {
+  gdn_decode_args_t a{};
+  a.q = dQ; a.k = dK; a.v = dV; a.g = dG; a.beta = dBeta;
+  a.state_in = dS_in; a.state_out = dS_out; a.o = dO;
+  a.q_sb = static_cast<int64_t>(H) * dk; a.q_sh = dk;
+  a.k_sb = a.q_sb; a.k_sh = dk;
+  a.v_sb = static_cast<int64_t>(H) * dv; a.v_sh = dv;
+  a.o_sb = a.v_sb; a.o_sh = dv;
+  a.g_sb = kda ? static_cast<int64_t>(H) * dk : H; a.g_sh = kda ? dk : 1;
+  a.beta_sb = H; a.beta_sh = 1;
+  a.B = B; a.Hqk = H; a.Hv = H; a.dk = dk; a.dv = dv;
+  a.io_dtype = io_dtype; a.g_dtype = io_dtype; a.beta_dtype = io_dtype;
+  a.gate_kind = kda ? GDN_GATE_LOG : GDN_GATE_LINEAR;
+  a.scale = 1.0f;
+  a.status = nullptr;
+  return a;
+}
+
+extern "C" int gdn_decode_ref_launch(int32_t B, int32_t H, int32_t dk, int32_t dv, const void* dQ,
+                                     const void* dK, const void* dV, const void* dAlpha,
+                                     const void* dBeta, const float* dS_in, float* dS_out, void* dO,
+                                     int32_t io_dtype, gdn_stream_t stream) {
+  const gdn_decode_args_t a =
+      ref_layout_args(B, H, dk, dv, dQ, dK, dV, dAlpha, dBeta, dS_in, dS_out, dO, io_dtype, false);
+  return gdn_decode_launch(&a, stream);
+}
+
+extern "C" int kda_decode_ref_launch(int32_t B, int32_t H, int32_t dk, int32_t dv, const void* dQ,
+                                     const void* dK, const void* dV, const void* dG,
+                                     const void* dBeta, const float* dS_in, float* dS_out, void* dO,
+                                     int32_t io_dtype, gdn_stream_t stream) {
+  const gdn_decode_args_t a =
+      ref_layout_args(B, H, dk, dv, dQ, dK, dV, dG, dBeta, dS_in, dS_out, dO, io_dtype, true);
+  return kda_decode_launch(&a, stream);
+}

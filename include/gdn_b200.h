@@ -1,0 +1,195 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) gated delta-rule library.
+ *
+ * The library implements three operations of the gated delta rule
+ * (GDN / KDA linear attention), each as hand-written sm_100a CUDA:
+ *
+ *   GDN decode (one token per sequence, scalar gate per head)
+ *       S      <- a * S                      a = exp(g) (log gate) or g (linear gate)
+ *       u      =  k^T S                       (per value column)
+ *       S      <- S + beta * k (v - u)^T
+ *       o      =  scale * S^T q
+ *   KDA decode: identical, but the gate is a d_k-vector, S <- diag(exp(g)) S.
+ *   GDN chunked prefill: the same recurrence over T tokens, computed chunk by
+ *       chunk (WY / UT transform) on the tcgen05 tensor cores.
+ *
+ * Conventions shared by every entry point
+ *   - Every pointer is a DEVICE pointer on the current CUDA device.  The caller
+ *     owns all memory; no entry point allocates device memory.
+ *   - The state is fp32, laid out [B, Hv, d_k, d_v] row-major (S[k][v]), and is
+ *     updated in place when state_out == state_in.
+ *   - q/k have Hqk heads, v/o/g/beta have Hv heads; Hv must be a multiple of
+ *     Hqk and value head h reads query/key head h / (Hv / Hqk)
+ *     (torch.repeat_interleave semantics).
+ *   - Launches are asynchronous and ordered on `stream` (a cudaStream_t; NULL
+ *     is the legacy default stream).  Every function is reentrant.
+ *   - Return value: 0 on success, else a GDN_ERR_* code; no entry point ever
+ *     aborts the process.  Failures detected on the device (a bounded wait
+ *     that timed out) are OR-ed into the optional `status` word as
+ *     GDN_DEVERR_* bits; the host reads it after synchronising.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_B200_ABI_VERSION 1
+
+typedef struct CUstream_st* gdn_stream_t; /* == cudaStream_t */
+
+/* element types */
+enum {
+  GDN_DT_F32 = 0,
+  GDN_DT_BF16 = 1,
+  GDN_DT_F16 = 2,
+};
+
+/* how `g` encodes the forget gate */
+enum {
+  GDN_GATE_LOG = 0,    /* decay = exp(g)   (BASELINE / FLA convention)           */
+  GDN_GATE_LINEAR = 1, /* decay = g        (the reference's `alpha` argument)    */
+};
+
+/* host-side return codes */
+enum {
+  GDN_OK = 0,
+  GDN_ERR_NULL = 1,        /* a required pointer is NULL                        */
+  GDN_ERR_SHAPE = 2,       /* unsupported or inconsistent sizes                 */
+  GDN_ERR_ALIGN = 3,       /* pointer or stride breaks 16-byte alignment        */
+  GDN_ERR_DTYPE = 4,       /* unsupported dtype / gate-kind combination         */
+  GDN_ERR_LAUNCH = 5,      /* the CUDA launch itself failed                     */
+  GDN_ERR_DEVICE = 6,      /* no device, or the device is not sm_100            */
+  GDN_ERR_WORKSPACE = 7,   /* workspace missing or too small                    */
+  GDN_ERR_DEVICE_WAIT = 8, /* a device-side wait timed out (from the status)    */
+};
+
+/* device-side status bits (OR-ed into *status) */
+enum {
+  GDN_DEVERR_FULL_TIMEOUT = 1u << 0,  /* consumer waited too long for a slab      */
+  GDN_DEVERR_EMPTY_TIMEOUT = 1u << 1, /* producer waited too long for a free slot */
+  GDN_DEVERR_MMA_TIMEOUT = 1u << 2,   /* tensor-core completion never signalled   */
+  GDN_DEVERR_DRAIN_TIMEOUT = 1u << 3, /* copies in flight never landed on abort   */
+};
+
+/*
+ * One decode step for a batch of sequences (GDN when g is [B,Hv], KDA when
+ * g is [B,Hv,d_k]).  Strides are in ELEMENTS and cover the (batch, head)
+ * axes; the innermost dimension of q/k/v/o (and of the KDA gate) must be
+ * contiguous.  Element strides times the element size must be multiples of
+ * 16 bytes and q/k/v/o/g base pointers 16-byte aligned (the rows are staged
+ * with cp.async.bulk).
+ */
+typedef struct {
+  const void* q;        /* [B, Hqk, d_k]   io_dtype                         */
+  const void* k;        /* [B, Hqk, d_k]   io_dtype                         */
+  const void* v;        /* [B, Hv,  d_v]   io_dtype                         */
+  const void* g;        /* GDN: [B, Hv]; KDA: [B, Hv, d_k]   g_dtype        */
+  const void* beta;     /* [B, Hv]         beta_dtype                       */
+  const float* state_in;/* [B, Hv, d_k, d_v] fp32 contiguous                */
+  float* state_out;     /* same layout; may equal state_in (in place)       */
+  void* o;              /* [B, Hv, d_v]    io_dtype                         */
+  int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh, o_sb, o_sh;
+  int64_t g_sb, g_sh, beta_sb, beta_sh;
+  int32_t B, Hqk, Hv, dk, dv;
+  int32_t io_dtype;     /* GDN_DT_BF16 or GDN_DT_F16                        */
+  int32_t g_dtype;      /* any GDN_DT_*                                      */
+  int32_t beta_dtype;   /* any GDN_DT_*                                      */
+  int32_t gate_kind;    /* GDN_GATE_LOG or GDN_GATE_LINEAR                   */
+  float scale;          /* output scale (1.0 = reference convention)         */
+  uint32_t* status;     /* optional device word for GDN_DEVERR_* bits        */
+} gdn_decode_args_t;
+
+/*
+ * Chunked prefill over T tokens.  Tensors are contiguous [B, T, H, d]
+ * (q/k: Hqk heads, v/o: Hv heads), g and beta contiguous [B, T, Hv].
+ * initial_state may be NULL (zero state).  final_state receives the state
+ * after token T-1.  T must be a multiple of chunk (64).
+ */
+typedef struct {
+  const void* q;            /* [B, T, Hqk, d_k] io_dtype                    */
+  const void* k;            /* [B, T, Hqk, d_k] io_dtype                    */
+  const void* v;            /* [B, T, Hv, d_v]  io_dtype                    */
+  const void* g;            /* [B, T, Hv]       g_dtype (log gate)          */
+  const void* beta;         /* [B, T, Hv]       beta_dtype                  */
+  const float* initial_state; /* [B, Hv, d_k, d_v] fp32 or NULL             */
+  float* final_state;       /* [B, Hv, d_k, d_v] fp32                       */
+  void* o;                  /* [B, T, Hv, d_v]  io_dtype                    */
+  int32_t B, T, Hqk, Hv, dk, dv, chunk;
+  int32_t io_dtype, g_dtype, beta_dtype;
+  float scale;
+  void* workspace;          /* device scratch, >= gdn_prefill_workspace_size */
+  size_t workspace_bytes;
+  uint32_t* status;
+} gdn_prefill_args_t;
+
+/* Library ABI version (GDN_B200_ABI_VERSION). */
+int gdn_abi_version(void);
+
+/* Human-readable text for a GDN_ERR_* code. */
+const char* gdn_status_string(int code);
+
+/*
+ * GDN decode step.  Replaces the reference's launcher
+ *   launch_gdn_dispatch   (cuda-attn-gdn/attn_gdn.cu:343-358,
+ *                          cuda-attn-gdn-tma/attn_gdn_tma.cu:521-545)
+ * and the cuTile kernel launch ct.launch(..., gdn_decode, (Q,K,V,Alpha,Beta,
+ * S_in,S_out,O)) (cutile-attn-gdn/main.py:116, 268-271), generalised to
+ * GQA head counts, bf16 I/O, a log gate and an in-place state.
+ */
+int gdn_decode_launch(const gdn_decode_args_t* args, gdn_stream_t stream);
+
+/*
+ * KDA decode step (per-channel gate g[B,Hv,d_k]).  Replaces
+ *   launch_kda_dispatch   (cuda-attn-kda/attn_kda.cu:327-345)
+ * and ct.launch(..., kda_decode, (Q,K,V,G,Beta,S_in,S_out,O))
+ * (cutile-attn-kda/main.py:206-269).
+ */
+int kda_decode_launch(const gdn_decode_args_t* args, gdn_stream_t stream);
+
+/*
+ * Reference-layout GDN decode: exactly the argument list of the reference's
+ * launch_gdn_dispatch(shape, dQ, dK, dV, dA, dB, dS_in, dS_out, dO, stream)
+ * (cuda-attn-gdn/attn_gdn.cu:343).  Q,K [B*H, d_k], V,O [B*H, d_v],
+ * Alpha,Beta [B*H] in io_dtype (f16 in the reference), alpha used directly
+ * (linear gate), S_in / S_out [B*H*d_k, d_v] fp32 (may alias).
+ */
+int gdn_decode_ref_launch(int32_t B, int32_t H, int32_t dk, int32_t dv,
+                          const void* dQ, const void* dK, const void* dV,
+                          const void* dAlpha, const void* dBeta,
+                          const float* dS_in, float* dS_out, void* dO,
+                          int32_t io_dtype, gdn_stream_t stream);
+
+/*
+ * Reference-layout KDA decode: the argument list of launch_kda_dispatch
+ * (cuda-attn-kda/attn_kda.cu:327).  G [B*H, d_k] is a log gate in io_dtype.
+ */
+int kda_decode_ref_launch(int32_t B, int32_t H, int32_t dk, int32_t dv,
+                          const void* dQ, const void* dK, const void* dV,
+                          const void* dG, const void* dBeta,
+                          const float* dS_in, float* dS_out, void* dO,
+                          int32_t io_dtype, gdn_stream_t stream);
+
+/*
+ * Device scratch the prefill needs for these arguments, in bytes (0 if none).
+ * The reference has no prefill; this is the new chunked path.
+ */
+size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args);
+
+/*
+ * GDN chunked prefill.  No reference counterpart exists (the reference only
+ * describes it: analysis/wave15-attention-research/MECHANISMS.md:398-445); its
+ * results are defined by T applications of the reference decode recurrence
+ * (analysis/wave15-attention-architecture/reference/pytorch_reference_gdn.py:38-91).
+ */
+int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */
