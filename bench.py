@@ -38,7 +38,7 @@ import __graft_entry__ as graft  # noqa: E402
 
 METRIC = "GDN decode state GB/s"
 UNIT = "GB/s"
-B, HQK, HV, D = 1024, 16, 32, 128
+B, HQK, HV, D = 1024, 16, 32, 128  # B is overridable with --batch (profiling runs)
 HBM_FALLBACK_GBS = 6650.0
 BF16_FALLBACK_TFLOPS = 1590.0
 
@@ -305,7 +305,7 @@ def run_gpu(args, world, rank, local):
                "sample": sample}
     if rank != 0:
         return
-    traffic = profiled_traffic("gdn_decode_B1024")
+    traffic = profiled_traffic(f"gdn_decode_B{B}")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -420,6 +420,7 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
 
 
 def main():
+    global B
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -428,9 +429,12 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=B,
+                    help="decode batch (default 1024, the headline; smaller for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    B = args.batch
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
