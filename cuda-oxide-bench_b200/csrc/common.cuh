@@ -1,6 +1,7 @@
 // common.cuh — host-side helpers shared by the launchers (device properties,
 // validation, alignment checks).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -23,6 +24,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline bool stride_ok(int64_t elems, int esize) { return ((elems * esize) & 15) == 0; }
 inline int host_dtype_size(int dt) { return dt == GDN_DT_F32 ? 4 : 2; }
 inline bool dtype_valid(int dt) { return dt == GDN_DT_F32 || dt == GDN_DT_BF16 || dt == GDN_DT_F16; }
+
+// Encodes (or returns a cached) 2-D fp32 tensor map over a row-major matrix
+// of `rows` x `cols` with a box of `box_rows` x `box_cols`.  Returns GDN_OK or
+// an error code.  The cache is keyed by every argument and guarded by a mutex.
+int fp32_tensor_map_2d(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows, uint32_t box_cols);
 
 // Raises the kernel's dynamic shared-memory limit once per device.
 template <typename Kernel>

@@ -20,7 +20,9 @@
 //     free ring slot, then stages the slab plus the q/k rows, the v slice and
 //     (KDA) the gate row into shared memory with cp.async.bulk, completing on
 //     the slot's "full" mbarrier.  A contiguous slab (BV == d_v) is a single
-//     bulk copy; otherwise one copy per state row.
+//     1-D bulk copy; a column block (BV < d_v) is a single 2-D TMA tile copy
+//     through a cached tensor map (one copy per row would serialise on the
+//     copy engine: 128 small copies per slab).
 //   warps 0-7 (consumers): wait "full", pull their rows of the slab into
 //     registers with 16-byte shared loads, release the slot ("empty"), then
 //     reduce k.S, q.S and q.k across rows (warp shuffles, then a ping-pong
@@ -32,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstring>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -73,7 +76,7 @@ struct DecodeTraits {
 
 template <int DK, int BV, typename IO, bool KDA>
 __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
-    decode_kernel(const DecodeParams p) {
+    decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap state_map) {
   using Tr = DecodeTraits<DK, BV, KDA>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -81,7 +84,8 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + Tr::kMaxStages);
   float* red = reinterpret_cast<float*>(smem + 256);  // [2][warps][2][BV]
   float* red_qk = red + 2 * Tr::kConsumerWarps * BV * 2;  // [2][warps]
-  unsigned char* ring = smem + Tr::kHeaderBytes;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem + Tr::kHeaderBytes) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -121,9 +125,8 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
       unsigned char* st = ring + static_cast<size_t>(stage) * p.stage_bytes;
       const float* src = a.state_in + (bh * DK) * a.dv + static_cast<int64_t>(vb) * BV;
       if (lane == 0) {
-        uint32_t bytes = 2 * Tr::kQKBytes + Tr::kVBytes;
+        uint32_t bytes = 2 * Tr::kQKBytes + Tr::kVBytes + Tr::kSlabBytes;
         if (KDA) bytes += p.g_row_bytes;
-        if (p.contiguous) bytes += Tr::kSlabBytes;
         mbar_expect_tx(&full[stage], bytes);
         const IO* q = static_cast<const IO*>(a.q) + b * a.q_sb + static_cast<int64_t>(hq) * a.q_sh;
         const IO* k = static_cast<const IO*>(a.k) + b * a.k_sb + static_cast<int64_t>(hq) * a.k_sh;
@@ -139,17 +142,10 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
           bulk_g2s(st + Tr::kSlabBytes + 2 * Tr::kQKBytes + Tr::kVBytes, g, p.g_row_bytes,
                    &full[stage]);
         }
-        if (p.contiguous) bulk_g2s(st, src, Tr::kSlabBytes, &full[stage]);
-      }
-      if (!p.contiguous) {
-        // one bulk copy per state row, spread over the warp's lanes
-        constexpr int kRowsPerLane = (DK + 31) / 32;
-        int mine = 0;
-        for (int r = lane; r < DK; r += 32) ++mine;
-        (void)kRowsPerLane;
-        if (mine) mbar_expect_tx(&full[stage], mine * BV * 4);
-        for (int r = lane; r < DK; r += 32)
-          bulk_g2s(st + r * BV * 4, src + static_cast<int64_t>(r) * a.dv, BV * 4, &full[stage]);
+        if (p.contiguous)
+          bulk_g2s(st, src, Tr::kSlabBytes, &full[stage]);
+        else  // x = first column (vb*BV*4 bytes: 16-byte aligned), y = first row
+          tma_load_2d(st, &state_map, vb * BV, static_cast<int>(bh * DK), &full[stage]);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[stage]);
@@ -312,10 +308,11 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  int stages = (di.smem_optin - static_cast<int>(Tr::kHeaderBytes)) / static_cast<int>(Tr::kStageBytes);
+  int stages =
+      (di.smem_optin - static_cast<int>(Tr::kHeaderBytes) - 128) / static_cast<int>(Tr::kStageBytes);
   if (stages > Tr::kMaxStages) stages = Tr::kMaxStages;
   if (stages < 2) return GDN_ERR_SHAPE;
-  const int smem = Tr::kHeaderBytes + stages * Tr::kStageBytes;
+  const int smem = Tr::kHeaderBytes + 128 + stages * Tr::kStageBytes;
   auto kern = decode_kernel<DK, BV, IO, KDA>;
   rc = ensure_smem_attr(kern, smem, attr_done);
   if (rc) return rc;
@@ -329,8 +326,14 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   p.stage_bytes = Tr::kStageBytes;
   p.contiguous = (BV == a.dv) ? 1 : 0;
   p.g_row_bytes = KDA ? DK * host_dtype_size(a.g_dtype) : 0;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  if (!p.contiguous) {
+    rc = fp32_tensor_map_2d(&map, a.state_in, static_cast<uint64_t>(a.B) * a.Hv * DK, a.dv, DK, BV);
+    if (rc) return rc;
+  }
   const int64_t grid64 = p.total_slabs < di.sm_count ? p.total_slabs : di.sm_count;
-  kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p);
+  kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p, map);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
@@ -366,14 +369,24 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
   return GDN_OK;
 }
 
-// Chooses the value-column block: whole rows when that still gives every SM
-// at least two slabs, otherwise 64-column blocks for better balance.
+// Chooses the value-column block: the widest block (whole rows when possible,
+// a single contiguous copy) that still gives every SM at least four slabs;
+// small batches fall back to narrower blocks for balance.
 static int pick_bv(const gdn_decode_args_t& a, int sm_count) {
-  if (a.dk <= 128 && a.dv % 128 == 0) {
-    const int64_t slabs128 = static_cast<int64_t>(a.B) * a.Hv * (a.dv / 128);
-    if (a.dk == 64 || slabs128 >= 2 * static_cast<int64_t>(sm_count)) return a.dk == 64 ? 64 : 128;
+  static const int kAllowed128[] = {128, 64, 32};
+  static const int kAllowed256[] = {64, 32};
+  const int* allowed = a.dk == 256 ? kAllowed256 : kAllowed128;
+  const int n = a.dk == 256 ? 2 : 3;
+  if (a.dk == 64) return 64;
+  int last = 0;
+  for (int i = 0; i < n; ++i) {
+    const int bv = allowed[i];
+    if (a.dv % bv) continue;
+    last = bv;
+    const int64_t slabs = static_cast<int64_t>(a.B) * a.Hv * (a.dv / bv);
+    if (slabs >= 4 * static_cast<int64_t>(sm_count)) return bv;
   }
-  return 64;
+  return last;
 }
 
 template <typename IO, bool KDA>
@@ -381,9 +394,12 @@ static int dispatch_dk(const gdn_decode_args_t& a, cudaStream_t stream, int bv) 
   switch (a.dk) {
     case 64: return launch_decode_impl<64, 64, IO, KDA>(a, stream);
     case 128:
-      return bv == 128 ? launch_decode_impl<128, 128, IO, KDA>(a, stream)
-                       : launch_decode_impl<128, 64, IO, KDA>(a, stream);
-    case 256: return launch_decode_impl<256, 64, IO, KDA>(a, stream);
+      if (bv == 128) return launch_decode_impl<128, 128, IO, KDA>(a, stream);
+      if (bv == 64) return launch_decode_impl<128, 64, IO, KDA>(a, stream);
+      return launch_decode_impl<128, 32, IO, KDA>(a, stream);
+    case 256:
+      return bv == 64 ? launch_decode_impl<256, 64, IO, KDA>(a, stream)
+                      : launch_decode_impl<256, 32, IO, KDA>(a, stream);
   }
   return GDN_ERR_SHAPE;
 }

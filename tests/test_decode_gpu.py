@@ -89,11 +89,13 @@ def test_golden_baseline_kda_16_steps(pkg, golden):
 
 
 @pytest.mark.parametrize("B,Hqk,Hv,d,steps", [
-    (8, 16, 32, 128, 64),     # config 0 (64-column slabs: few heads)
-    (64, 16, 32, 128, 4),     # config 1 smallest batch (whole-row slabs)
+    (8, 16, 32, 128, 64),     # config 0 (32-column TMA tile slabs: few heads)
+    (10, 16, 32, 128, 4),     # 64-column TMA tile slabs
+    (64, 16, 32, 128, 4),     # config 1 smallest batch (whole-row bulk-copy slabs)
     (3, 1, 4, 128, 8),        # group of 4, ragged batch
     (2, 2, 2, 64, 8),         # d = 64
-    (1, 2, 4, 256, 4),        # d = 256 (reference qwen3 head size)
+    (1, 2, 4, 256, 4),        # d = 256 (reference qwen3 head size), 32-column slabs
+    (40, 2, 4, 256, 2),       # d = 256, 64-column slabs
 ])
 def test_gdn_decode_matches_oracle(pkg, inputs, orc, B, Hqk, Hv, d, steps):
     x = inputs.make_decode_inputs(steps, B, Hqk, Hv, d, seed=B * 7 + d)
