@@ -56,26 +56,34 @@ EncodeTiledFn encode_fn() {
 
 struct MapKey {
   const void* base;
-  uint64_t rows, cols;
-  uint32_t box_rows, box_cols;
-  int dev;
-  bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
-           box_cols == o.box_cols && dev == o.dev;
-  }
+  int dev, dtype, rank, swizzle;
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
 
 }  // namespace
 
-int fp32_tensor_map_2d(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
-                       uint32_t box_rows, uint32_t box_cols) {
+int tensor_map(CUtensorMap* out, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+               const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+               CUtensorMapSwizzle swizzle) {
   static std::mutex mu;
-  static MapKey keys[32];
-  static CUtensorMap maps[32];
+  static MapKey keys[64];
+  static CUtensorMap maps[64];
   static int used = 0, next = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_DEVICE;
-  const MapKey key{base, rows, cols, box_rows, box_cols, dev};
+  if (rank < 1 || rank > 5) return GDN_ERR_SHAPE;
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  if (cudaGetDevice(&key.dev) != cudaSuccess) return GDN_ERR_DEVICE;
+  key.base = base;
+  key.dtype = static_cast<int>(dtype);
+  key.rank = static_cast<int>(rank);
+  key.swizzle = static_cast<int>(swizzle);
+  for (uint32_t i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) key.strides[i] = strides[i];
+  }
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i)
     if (keys[i] == key) {
@@ -86,19 +94,32 @@ int fp32_tensor_map_2d(CUtensorMap* out, const void* base, uint64_t rows, uint64
   if (!fn) return GDN_ERR_DEVICE;
   CUtensorMap m;
   std::memset(&m, 0, sizeof(m));
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 4};
-  const cuuint32_t box[2] = {box_cols, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  if (fn(&m, dtype, rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return GDN_ERR_SHAPE;
-  const int slot = used < 32 ? used++ : (next++ & 31);
+  const int slot = used < 64 ? used++ : (next++ & 63);
   keys[slot] = key;
   maps[slot] = m;
   *out = m;
   return GDN_OK;
+}
+
+int fp32_tensor_map_2d(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows, uint32_t box_cols) {
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {cols * 4};
+  const uint32_t box[2] = {box_cols, box_rows};
+  return tensor_map(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace gdn

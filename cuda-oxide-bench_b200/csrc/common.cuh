@@ -31,6 +31,12 @@ inline bool dtype_valid(int dt) { return dt == GDN_DT_F32 || dt == GDN_DT_BF16 |
 int fp32_tensor_map_2d(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
                        uint32_t box_rows, uint32_t box_cols);
 
+// General tiled tensor map (cached likewise); strides are in bytes for
+// dimensions 1..rank-1, dims/box innermost first.  No interleave, zero OOB fill.
+int tensor_map(CUtensorMap* out, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+               const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+               CUtensorMapSwizzle swizzle);
+
 // Raises the kernel's dynamic shared-memory limit once per device.
 template <typename Kernel>
 int ensure_smem_attr(Kernel k, int bytes, std::atomic<uint64_t>& done_mask) {
