@@ -419,6 +419,43 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
     return ex
 
 
+def run_prefill(args, world, rank, local):
+    """BASELINE config 3 (B=4, T=4096, Hqk=16, Hv=32, chunk 64) as its own
+    line: chunked-form TFLOP/s, device-timed; used for profiling the prefill."""
+    pkg = graft.package()
+    inputs = graft.submodule("inputs")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    Bp, Tp = 4, 4096
+    p = inputs.make_prefill_inputs(Bp, Tp, HQK, HV, D, seed=3, device=dev)
+    fs = torch.empty((Bp, HV, D, D), dtype=torch.float32, device=dev)
+    po = torch.empty((Bp, Tp, HV, D), dtype=torch.bfloat16, device=dev)
+    fn = lambda: pkg.gdn_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+    for _ in range(args.warmup):
+        fn()
+    pkg.check_device_status(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.steps
+    hbm, bf16, kind = peaks()
+    fl = inputs.gdn_prefill_flops(Bp, Tp, HQK, HV, D, 64)
+    tf = fl / (ms * 1e-3) / 1e12
+    if rank == 0:
+        print(json.dumps({"metric": "GDN prefill chunked-form TFLOP/s", "value": round(tf, 2),
+                          "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": args.steps,
+                          "warmup": args.warmup, "n_gpus": world,
+                          "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": bf16,
+                                       "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
+                                       "peak_kind": f"{kind} (burst bf16 GEMM)"},
+                          "config": {"workload": "GDN prefill B=4 T=4096 Hqk=16 Hv=32 d=128 C=64"}}),
+              flush=True)
+
+
 def main():
     global B
     ap = argparse.ArgumentParser()
@@ -429,6 +466,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="decode", choices=("decode", "prefill"),
+                    help="decode (headline, configs[1]/4) or prefill (config 3, for profiling)")
     ap.add_argument("--batch", type=int, default=B,
                     help="decode batch (default 1024, the headline; smaller for ncu captures)")
     args = ap.parse_args()
@@ -439,6 +478,9 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "prefill":
+            graft.build()
+            run_prefill(args, world, rank, local)
         else:
             graft.build()
             run_gpu(args, world, rank, local)
