@@ -221,18 +221,44 @@ def run_gpu(args, world, rank, local):
         x = inputs.make_decode_inputs(1, B, hq, hv, D, seed=100 * rank + i, device=dev,
                                       state_std=0.0)
         toks.append([x.q[0], x.k[0], x.v[0], x.g[0], x.beta[0]])
-    out = torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev)
-    steps = [pkg.DecodeStep(*t, state, out=out) for t in toks]
-    gather_buf = torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    # two output buffers: the all-gather of step i (NCCL stream) overlaps the
+    # decode of step i + 1; step i + 2 waits for it before reusing the buffer
+    outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    out = outs[0]
+    res = args.sm_reserve if world > 1 else 0
+    steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
+    steps2 = [pkg.DecodeStep(*t, state, out=outs[1], sm_reserve=res) for t in toks]
+    gbufs = [torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)] \
+        if world > 1 else None
+    gather_buf = gbufs[0] if world > 1 else None
+    works = [None, None]
+
+    def launch(i):
+        (steps if i % 2 == 0 else steps2)[i % pool]()
+
+    def gather(i):
+        if world > 1:
+            works[i % 2] = dist.all_gather_into_tensor(gbufs[i % 2].view(-1), outs[i % 2].view(-1),
+                                                       async_op=True)
+
+    def settle(i):
+        w = works[i % 2]
+        if w is not None:
+            w.wait()
+            works[i % 2] = None
 
     def one_step(i):
-        steps[i % pool]()
-        if world > 1:
-            dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
+        settle(i)
+        launch(i)
+        gather(i)
+        if args.no_overlap:
+            settle(i)
 
     stream = torch.cuda.current_stream(dev)
     for i in range(args.warmup):
         one_step(i)
+    settle(args.warmup)
+    settle(args.warmup + 1)
     pkg.check_device_status(dev)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -242,11 +268,15 @@ def run_gpu(args, world, rank, local):
     with ClockSampler(local) as clk:
         e0.record(stream)
         for i in range(args.steps):
+            settle(i)
             kev[i][0].record(stream)
-            steps[i % pool]()
+            launch(i)
             kev[i][1].record(stream)
-            if world > 1:
-                dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
+            gather(i)
+            if args.no_overlap:
+                settle(i)
+        settle(args.steps)
+        settle(args.steps + 1)
         e1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
@@ -318,7 +348,7 @@ def run_gpu(args, world, rank, local):
                                                                  if world > 1 else ""),
                    "l2": "inputs larger than L2 (4.3 GB state), no flush"},
         "tokens_per_s": round(B / (ms * 1e-3), 1),
-        "pct_of_8TBs": round(100 * value / 8000.0, 2),
+        "pct_of_8TBs_per_gpu": round(100 * value / world / 8000.0, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic,
                      "peak_kind": f"{peak_kind} (burst copy)",
@@ -327,6 +357,8 @@ def run_gpu(args, world, rank, local):
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": args.steps,
+        "allgather_overlapped": world > 1 and not args.no_overlap,
+        "sm_reserve": res,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "extras": extras,
@@ -466,6 +498,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sm-reserve", type=int, default=16,
+                    help="SMs the decode leaves to the overlapped all-gather (N>1)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="N>1: run each step's all-gather after its decode, not overlapped")
     ap.add_argument("--workload", default="decode", choices=("decode", "prefill"),
                     help="decode (headline, configs[1]/4) or prefill (config 3, for profiling)")
     ap.add_argument("--batch", type=int, default=B,

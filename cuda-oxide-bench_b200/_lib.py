@@ -64,6 +64,7 @@ class DecodeArgs(ctypes.Structure):
         ("beta_dtype", ctypes.c_int32), ("gate_kind", ctypes.c_int32),
         ("scale", ctypes.c_float),
         ("status", ctypes.c_void_p),
+        ("sm_reserve", ctypes.c_int32),
     ]
 
 

@@ -62,7 +62,8 @@ def _stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda) -> _lib.DecodeArgs:
+def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
+                 sm_reserve: int = 0) -> _lib.DecodeArgs:
     if q.dim() != 3 or k.shape != q.shape or v.dim() != 3:
         raise GDNError("q, k must be [B, Hqk, d_k] and v [B, Hv, d_v]", 2)
     B, Hqk, dk = q.shape
@@ -108,6 +109,7 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda) -> _li
     a.gate_kind = _lib.GATE_LOG if gate == "log" else _lib.GATE_LINEAR
     a.scale = float(scale)
     a.status = status_word(q.device).data_ptr()
+    a.sm_reserve = int(sm_reserve)
     return a
 
 
@@ -118,13 +120,14 @@ class DecodeStep:
     must stay alive and in place while the object is used."""
 
     def __init__(self, q, k, v, g, beta, state, *, out=None, state_out=None, scale=1.0,
-                 gate="log", kda=False):
+                 gate="log", kda=False, sm_reserve=0):
         dev = _require_cuda(q, k, v, g, beta, state)
         self.out = out if out is not None else torch.empty(
             (v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
         state_out = state if state_out is None else state_out
         self._keep = (q, k, v, g, beta, state, state_out, self.out)
-        self._args = _decode_args(q, k, v, g, beta, state, state_out, self.out, scale, gate, kda)
+        self._args = _decode_args(q, k, v, g, beta, state, state_out, self.out, scale, gate, kda,
+                                  sm_reserve)
         self._argp = ctypes.byref(self._args)
         L = _lib.load()
         self._fn = L.kda_decode_launch if kda else L.gdn_decode_launch
@@ -139,19 +142,21 @@ class DecodeStep:
 
 
 def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: str = "log",
-               state_out=None, check: bool = False) -> torch.Tensor:
+               state_out=None, check: bool = False, sm_reserve: int = 0) -> torch.Tensor:
     """One GDN decode step; ``state`` is updated in place (or written to
     ``state_out``).  Returns o [B, Hv, d_v] in q's dtype.
 
     q, k [B, Hqk, d_k] bf16/f16; v [B, Hv, d_v]; g, beta [B, Hv] (any float
     dtype; ``gate='log'`` means decay = exp(g)); state fp32 [B, Hv, d_k, d_v].
     ``check=True`` synchronises and raises on a device-side failure.
+    ``sm_reserve`` leaves that many SMs free for a concurrent kernel (the
+    persistent decode otherwise occupies every SM).
     """
     dev = _require_cuda(q, k, v, g, beta, state)
     if out is None:
         out = torch.empty((v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
     so = state if state_out is None else state_out
-    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, False)
+    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, False, sm_reserve)
     _lib.check(_lib.load().gdn_decode_launch(ctypes.byref(a), _stream_ptr(dev)), "gdn_decode")
     if check:
         check_device_status(dev)

@@ -332,7 +332,9 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
     rc = fp32_tensor_map_2d(&map, a.state_in, static_cast<uint64_t>(a.B) * a.Hv * DK, a.dv, DK, BV);
     if (rc) return rc;
   }
-  const int64_t grid64 = p.total_slabs < di.sm_count ? p.total_slabs : di.sm_count;
+  int ctas = di.sm_count - (a.sm_reserve > 0 ? a.sm_reserve : 0);
+  if (ctas < 1) ctas = 1;
+  const int64_t grid64 = p.total_slabs < ctas ? p.total_slabs : ctas;
   kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p, map);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

@@ -102,13 +102,18 @@ typedef struct {
   int32_t gate_kind;    /* GDN_GATE_LOG or GDN_GATE_LINEAR                   */
   float scale;          /* output scale (1.0 = reference convention)         */
   uint32_t* status;     /* optional device word for GDN_DEVERR_* bits        */
+  int32_t sm_reserve;   /* SMs left free for concurrent kernels (e.g. an     */
+                        /* NCCL collective overlapping the step); 0 = none   */
 } gdn_decode_args_t;
 
 /*
  * Chunked prefill over T tokens.  Tensors are contiguous [B, T, H, d]
  * (q/k: Hqk heads, v/o: Hv heads), g and beta contiguous [B, T, Hv].
  * initial_state may be NULL (zero state).  final_state receives the state
- * after token T-1.  T must be a multiple of chunk (64).
+ * after token T-1.  chunk must be 64; T may be any length >= 1 (the last
+ * chunk is zero-padded, which leaves state and outputs unchanged).
+ * d_k = d_v = 128.  No workspace is needed (gdn_prefill_workspace_size
+ * returns 0).
  */
 typedef struct {
   const void* q;            /* [B, T, Hqk, d_k] io_dtype                    */

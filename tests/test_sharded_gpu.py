@@ -1,0 +1,76 @@
+"""Value-head-sharded decode on 2 GPUs over NCCL: the gathered outputs and the
+per-rank state shards match the single-GPU decode of all heads.  Skipped with
+fewer than two GPUs."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import graft
+
+pytestmark = pytest.mark.gpu
+
+B, HQK, HV, D, STEPS = 64, 16, 32, 128, 8
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        pkg = graft.package()
+        inputs = graft.submodule("inputs")
+        sh = graft.submodule("sharded")
+        x = inputs.make_decode_inputs(STEPS, B, HQK, HV, D, seed=17)
+        s = sh.shard_heads(HV, HQK, world, rank)
+        dev = torch.device("cuda", rank)
+        dec = sh.ShardedGDNDecoder(B, HQK, HV, D, D, device=dev,
+                                   state=x.state[:, s.h0:s.h1].contiguous().to(dev))
+        outs = []
+        for t in range(STEPS):
+            o = dec.step(x.q[t].to(dev), x.k[t].to(dev), x.v[t].to(dev), x.g[t].to(dev),
+                         x.beta[t].to(dev), gather=True)
+            outs.append(o.float().cpu())
+        pkg.check_device_status(dev)
+        states = [torch.empty_like(dec.state) for _ in range(world)]
+        dist.all_gather(states, dec.state)
+        if rank == 0:
+            q.put((torch.stack(outs).numpy(), torch.cat([t.cpu() for t in states], 1).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_sharded_decode_two_gpus_matches_single(pkg, inputs):
+    x = inputs.make_decode_inputs(STEPS, B, HQK, HV, D, seed=17)
+    st = x.state.to("cuda:0")
+    ref = []
+    for t in range(STEPS):
+        ref.append(pkg.gdn_decode(x.q[t].cuda(), x.k[t].cuda(), x.v[t].cuda(), x.g[t].cuda(),
+                                  x.beta[t].cuda(), st).float().cpu())
+    ref_o, ref_s = torch.stack(ref).numpy(), st.cpu().numpy()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    o, s = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    np.testing.assert_allclose(o, ref_o, rtol=1e-2, atol=1e-2)
+    assert np.abs(s - ref_s).max() < 1e-5
