@@ -16,17 +16,26 @@
 //
 // Every product is a tcgen05.mma with M = 128, written transposed so the 128
 // TMEM lanes index d_v (or d_k): [K;Q] K^T, W^T = K^T T_w^T, U^T = V^T T_u^T,
-// X^T = S^T W^T, Z^T = S^T Q^T, O_intra^T = V'^T P^T, dS^T = V''^T K.
-// Operands are bf16 (f16) in 128B-swizzled shared memory; TMA fills the
-// K/Q/V tiles and the same tile serves as K-major and MN-major operand.
-// Accumulators live in TMEM (512 columns); the fp32 master state lives in
-// registers (thread = one d_v row of S^T, 64 of its d_k columns).
+// V'^T = U^T - S^T W^T (accumulated with a negated A onto U), Z^T = S^T Q^T,
+// O_intra^T = V'^T P^T, dS^T = V''^T K.  Operands are bf16 (f16) in
+// 128B-swizzled shared memory (TMA fills K/Q/V; one tile serves as K-major and
+// MN-major operand), except S^T, which lives in TMEM as bf16 and is read as
+// the A operand.  Accumulators use all 512 TMEM columns; the fp32 master state
+// lives in registers of the state warps.
 // Precision: the decayed V'' = diag(exp(G_C - G_j)) V' that updates the state
 // is split into bf16 hi + lo halves (two MMAs), and K enters the state update
 // unscaled, so the state accumulates with ~16 mantissa bits per term.
 //
-// One CTA per (batch, value head), 256 threads (8 warps).  Warp w reads TMEM
-// lane quarter w % 4; warps w and w + 4 split the columns.
+// One CTA per (batch, value head), 12 warps in two roles that run
+// concurrently, one chunk apart:
+//   intra (warps 0-3):   KQ MMA, A and P rows, T = (I+A)^-1, W/U MMAs, W^T tile
+//                        for chunk c+1 ...
+//   state (warps 4-11):  ... while the state chain of chunk c runs: V' = U - W S,
+//                        V'/V'' tiles, O_intra/dS MMAs, state update, outputs.
+// K/Q/V are double-buffered; the state warps' MMA thread refills a slot with
+// chunk c+2 by TMA as soon as chunk c's last MMA on it has completed.
+// Hand-offs use mbarriers (TMA completion, tcgen05.commit, group arrivals); every
+// wait is bounded and each group agrees on an abort before leaving its loop.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -42,11 +51,11 @@ namespace prefill {
 
 #ifdef GDN_PREFILL_TRACE
 // Phase timestamps of CTA 0 (profiling builds only): [chunk][phase].
-__device__ unsigned long long g_trace[64 * 12];
-#define TRACE(c, ph)                                                              \
-  do {                                                                            \
-    if (blockIdx.x == 0 && threadIdx.x == 0 && (c) < 64) g_trace[(c) * 12 + (ph)] = \
-        global_timer_ns();                                                        \
+__device__ unsigned long long g_trace[64 * 16];
+#define TRACE(c, ph)                                                                           \
+  do {                                                                                         \
+    if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x == 0 || threadIdx.x == 128))              \
+      g_trace[(c) * 16 + (ph)] = global_timer_ns();                                            \
   } while (0)
 #else
 #define TRACE(c, ph) \
@@ -56,39 +65,54 @@ __device__ unsigned long long g_trace[64 * 12];
 
 constexpr int kC = 64;     // chunk length
 constexpr int kD = 128;    // d_k = d_v
-constexpr int kThreads = 256;
+constexpr int kIntraThreads = 128;
+constexpr int kStateThreads = 256;
+constexpr int kThreads = kIntraThreads + kStateThreads;
+constexpr int kBarIntra = 1, kBarState = 2;  // named barrier ids
 
 // shared-memory map (byte offsets from a 1024-aligned base)
-constexpr uint32_t kKQ = 0;            // 2 buffers x [K | Q] tile: 2 d_k blocks x (K 8 KB + Q 8 KB)
-constexpr uint32_t kKQBuf = 32768;
+constexpr uint32_t kKQ = 0;            // 2 slots x [K | Q] tile: 2 d_k blocks x (K 8 KB + Q 8 KB)
+constexpr uint32_t kKQSlot = 32768;
 constexpr uint32_t kKQBlock = 16384;
-constexpr uint32_t kV = 65536;         // 2 buffers x V tile: 2 d_v blocks x 8 KB
-constexpr uint32_t kVBuf = 16384;
+constexpr uint32_t kV = 65536;         // 2 slots x V tile: 2 d_v blocks x 8 KB
+constexpr uint32_t kVSlot = 16384;
 constexpr uint32_t kVBlock = 8192;
 constexpr uint32_t kTw = 98304;        // T diag(beta gamma), K-major rows i   (8 KB)
 constexpr uint32_t kTu = 106496;       // T diag(beta), K-major rows i          (8 KB)
-constexpr uint32_t kP = 114688;        // causal decayed QK^T, rows i           (8 KB)
-constexpr uint32_t kWT = 122880;       // W^T, MN-major rows d_k               (16 KB)
-constexpr uint32_t kST = 139264;       // S^T bf16, K-major rows d_v, 2 blocks (32 KB)
-constexpr uint32_t kSTBlock = 16384;
-constexpr uint32_t kVP = 172032;       // V'^T, K-major rows d_v               (16 KB)
-constexpr uint32_t kVH = 188416;       // V''^T hi                             (16 KB)
-constexpr uint32_t kVL = 204800;       // V''^T lo                             (16 KB)
-// fp32 solver matrices (row stride 68 floats) alias V'/V''hi/V''lo, which are
-// dead between the previous chunk's last MMA and this chunk's epilogue.
-constexpr int kLd = 68;
-constexpr uint32_t kAf = kVP;                       // A   [64][68]
-constexpr uint32_t kTf = kVP + 64 * kLd * 4;        // T   [64][68]
-constexpr uint32_t kMs = kVP + 2 * 64 * kLd * 4;    // merge scratch (32 x 68 floats)
-constexpr uint32_t kVec = 221184;      // 4 x 64 fp32: G, gamma, beta, raw g
-constexpr uint32_t kBars = kVec + 1024;
-constexpr uint32_t kSmemBytes = kBars + 64;
+constexpr uint32_t kP = 114688;        // 2 slots x causal decayed QK^T        (8 KB each)
+constexpr uint32_t kPSlot = 8192;
+constexpr uint32_t kWT = 131072;       // W^T, MN-major rows d_k               (16 KB)
+constexpr uint32_t kVP = 147456;       // V'^T, K-major rows d_v               (16 KB)
+constexpr uint32_t kVH = 163840;       // V''^T hi                             (16 KB)
+constexpr uint32_t kVL = 180224;       // V''^T lo                             (16 KB)
+constexpr int kLd = 68;                // fp32 row stride of the solver matrices
+constexpr uint32_t kAT = 196608;       // A, overwritten in place by T: [64][68] fp32
+constexpr uint32_t kMs = kTw;          // solver scratch [32][68] fp32 (aliases T_w/T_u,
+                                       // which are written only after the solve)
+constexpr uint32_t kVec = kAT + 64 * kLd * 4;  // 3 slots x {G, gamma, beta, decay} x 64 fp32
+constexpr int kVecSlot = 4 * 64;               // floats per slot
+constexpr uint32_t kBars = kVec + 3 * kVecSlot * 4;
+constexpr uint32_t kSmemBytes = kBars + 256;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // + alignment slack
-static_assert(kMs + 32 * kLd * 4 <= kVL + 16384, "solver scratch overflows its alias");
+static_assert(32 * kLd * 4 <= 2 * 8192, "solver scratch overflows its alias");
 
 // TMEM columns
-constexpr uint32_t kTmKQ = 0, kTmZ = 64, kTmW = 128, kTmU = 192, kTmX = 256, kTmOI = 320,
-                   kTmDS = 384, kTmCols = 512;
+constexpr uint32_t kTmST = 0;    // S^T bf16, packed pairs: 64 columns
+constexpr uint32_t kTmKQ = 64;   // [K;Q]K^T, then reused for W^T
+constexpr uint32_t kTmU = 128;   // 2 slots x U^T / V'^T
+constexpr uint32_t kTmZ = 256, kTmOI = 320, kTmDS = 384, kTmCols = 512;
+
+// mbarrier indices
+enum {
+  kBarKQV = 0,        // [2] TMA of a K/Q/V slot landed
+  kBarIMma = 2,       // intra MMA completion
+  kBarReady = 3,      // [2] intra -> state: W^T tile, U, P, gates of a chunk ready
+  kBarX = 5,          // V' = U - W S done (W^T tile free)
+  kBarZ = 6,          // Z done
+  kBarS2 = 7,         // O_intra and dS done
+  kBarSlotFree = 8,   // [2] a K/Q/V, U and P slot may be refilled
+  kNumBars = 10,
+};
 
 struct Params {
   gdn_prefill_args_t a;
@@ -105,20 +129,25 @@ __device__ __forceinline__ void store_row16(uint32_t tile, int row, int chunk0, 
              tc::pack2<BF16>(v[14], v[15]));
 }
 
-// Every thread waits (bounded) on the barrier phase; the CTA then agrees on
-// the outcome, so a timeout unwinds all threads together.
-__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
-  const bool ok = mbar_wait_bounded(bar, parity);
-  return __syncthreads_and(ok) != 0;
+// Bounded wait polled by lane 0 of each warp (the other lanes sleep in the
+// barrier instead of competing for issue slots), then a group-wide vote: the
+// group leaves together if any warp timed out (no thread is stranded at a
+// barrier).  The barrier also orders the waiters' later reads after the phase.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int bar_id, int count) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity);
+  return !named_barrier_or(bar_id, count, !ok);
 }
 
 // ------------------------------------------------------------ triangular solve
 // m16n8k8 TF32 warp MMA with the 3xTF32 split (hi*hi + hi*lo + lo*hi), which
-// keeps the block products of the solve at close to fp32 accuracy.
+// keeps the block products of the solve at close to fp32 accuracy.  hi keeps
+// the top 19 bits of x (exactly representable in tf32) and lo = x - hi is
+// exact in fp32; the tensor core reads only the tf32 bits of lo.  Bit masking
+// keeps the split on the integer pipe.
 __device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
-  const float r = x - __uint_as_float(hi);
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+  hi = __float_as_uint(x) & 0xFFFFE000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
 }
 
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -161,77 +190,81 @@ __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], 
   }
 }
 
-// T = (I + A)^-1 for strictly lower-triangular A (64 x 64 fp32, stride kLd).
-// 1) the four 16 x 16 diagonal blocks D_r by forward substitution (one warp
-//    per block, one lane per column, fp32);  2) T_10 = -D_1 A_10 D_0 and
-// T_32 = -D_3 A_32 D_2;  3) the lower-left 32 x 32 quadrant
-// -T_bot A_bl T_top.  The block products run on m16n8k8 TF32 warp MMAs.
-// Only the lower triangle of T is written.
-__device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* M, int tid) {
-  const int warp = tid >> 5, lane = tid & 31;
-  if (warp < 4) {
-    if (lane < 16) {
-      const int bb = warp * 16, c = lane;
-      float t[16];
+// In place: AT holds strictly-lower A (64 x 64 fp32, stride kLd, zeros on and
+// above the diagonal) and is overwritten with T = (I + A)^-1.  Run by the 4
+// intra warps (128 threads).  Steps: the four 16 x 16 diagonal blocks D_r by
+// forward substitution (one warp each, one lane per column, fp32); T_10 =
+// -D_1 A_10 D_0 and T_32 = -D_3 A_32 D_2; then the lower-left quadrant
+// -T_bot A_bl T_top through Y = A_bl T_top.  Each block of A is last read
+// before the block of T that replaces it is written.
+__device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, int lane) {
+  {
+    const int bb = warp * 16, c = lane & 15;
+    float t[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) t[i] = (i == c) ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) t[i] = (i == c) ? 1.f : 0.f;
 #pragma unroll
-      for (int i = 1; i < 16; ++i) {
-        const float* row = A + (bb + i) * kLd + bb;
-        float acc = 0.f;
+    for (int i = 1; i < 16; ++i) {
+      const float* row = AT + (bb + i) * kLd + bb;
+      float acc = 0.f;
 #pragma unroll
-        for (int j4 = 0; j4 < i; j4 += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(row + j4);
-          acc = fmaf(a4.x, t[j4], acc);
-          if (j4 + 1 < i) acc = fmaf(a4.y, t[j4 + 1], acc);
-          if (j4 + 2 < i) acc = fmaf(a4.z, t[j4 + 2], acc);
-          if (j4 + 3 < i) acc = fmaf(a4.w, t[j4 + 3], acc);
-        }
-        t[i] -= acc;
+      for (int j4 = 0; j4 < i; j4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(row + j4);
+        acc = fmaf(a4.x, t[j4], acc);
+        if (j4 + 1 < i) acc = fmaf(a4.y, t[j4 + 1], acc);
+        if (j4 + 2 < i) acc = fmaf(a4.z, t[j4 + 2], acc);
+        if (j4 + 3 < i) acc = fmaf(a4.w, t[j4 + 3], acc);
       }
+      t[i] -= acc;
+    }
+    __syncwarp();
+    if (lane < 16) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) T[(bb + i) * kLd + bb + c] = t[i];
+      for (int i = 0; i < 16; ++i) AT[(bb + i) * kLd + bb + c] = t[i];
     }
   }
-  __syncthreads();
-  // level 1: warps 0 and 1 build T_10 and T_32 (X = A_rc D_c in scratch, then -D_r X)
-  if (warp < 2) {
+  tc::group_sync(kBarIntra, kIntraThreads);
+  if (warp < 2) {  // T_10 (warp 0) and T_32 (warp 1)
     const int c = warp * 2, r = c + 1;
     float* X = M + warp * 16 * kLd;
     float acc[2][4] = {};
-    block_mma(acc, A + 16 * r * kLd + 16 * c, T + 16 * c * kLd + 16 * c, lane);
+    block_mma(acc, AT + 16 * r * kLd + 16 * c, AT + 16 * c * kLd + 16 * c, lane);
     block_store(X, acc, 1.f, lane);
     __syncwarp();
     float acc2[2][4] = {};
-    block_mma(acc2, T + 16 * r * kLd + 16 * r, X, lane);
-    block_store(T + 16 * r * kLd + 16 * c, acc2, -1.f, lane);
+    block_mma(acc2, AT + 16 * r * kLd + 16 * r, X, lane);
+    block_store(AT + 16 * r * kLd + 16 * c, acc2, -1.f, lane);
   }
-  __syncthreads();
-  // level 2: warp (r-2)*2 + c builds Y_rc = sum_k A_rk T_kc over the top blocks
-  if (warp < 4) {
+  tc::group_sync(kBarIntra, kIntraThreads);
+  {  // Y_rc = sum_k A_rk T_kc over the top blocks, warp (r-2)*2 + c
     const int r = 2 + (warp >> 1), c = warp & 1;
     float acc[2][4] = {};
     if (c == 0) {
-      block_mma(acc, A + 16 * r * kLd + 0, T + 0, lane);                         // A_r0 D_0
-      block_mma(acc, A + 16 * r * kLd + 16, T + 16 * kLd + 0, lane);             // A_r1 T_10
+      block_mma(acc, AT + 16 * r * kLd + 0, AT + 0, lane);                      // A_r0 D_0
+      block_mma(acc, AT + 16 * r * kLd + 16, AT + 16 * kLd + 0, lane);          // A_r1 T_10
     } else {
-      block_mma(acc, A + 16 * r * kLd + 16, T + 16 * kLd + 16, lane);            // A_r1 D_1
+      block_mma(acc, AT + 16 * r * kLd + 16, AT + 16 * kLd + 16, lane);         // A_r1 D_1
     }
     block_store(M + (r - 2) * 16 * kLd + 16 * c, acc, 1.f, lane);
   }
-  __syncthreads();
-  if (warp < 4) {
+  tc::group_sync(kBarIntra, kIntraThreads);
+  {
     const int r = 2 + (warp >> 1), c = warp & 1;
     float acc[2][4] = {};
     if (r == 2) {
-      block_mma(acc, T + 32 * kLd + 32, M + 16 * c, lane);                       // D_2 Y_2c
+      block_mma(acc, AT + 32 * kLd + 32, M + 16 * c, lane);                     // D_2 Y_2c
     } else {
-      block_mma(acc, T + 48 * kLd + 32, M + 16 * c, lane);                       // T_32 Y_2c
-      block_mma(acc, T + 48 * kLd + 48, M + 16 * kLd + 16 * c, lane);            // D_3 Y_3c
+      block_mma(acc, AT + 48 * kLd + 32, M + 16 * c, lane);                     // T_32 Y_2c
+      block_mma(acc, AT + 48 * kLd + 48, M + 16 * kLd + 16 * c, lane);          // D_3 Y_3c
     }
-    block_store(T + 16 * r * kLd + 16 * c, acc, -1.f, lane);
+    block_store(AT + 16 * r * kLd + 16 * c, acc, -1.f, lane);
   }
-  __syncthreads();
+  tc::group_sync(kBarIntra, kIntraThreads);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
+  return tc::pack2<BF16>(lo, hi);
 }
 
 template <bool BF16>
@@ -244,309 +277,253 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
-  float* sG = reinterpret_cast<float*>(smem + kVec);
-  float* sGam = sG + 64;
-  float* sBeta = sG + 128;
-  float* sGraw = sG + 192;
-  float* Af = reinterpret_cast<float*>(smem + kAf);
-  float* Tf = reinterpret_cast<float*>(smem + kTf);
+  float* vec = reinterpret_cast<float*>(smem + kVec);  // [slot][G | gamma | beta][64]
+  float* AT = reinterpret_cast<float*>(smem + kAT);
   float* Ms = reinterpret_cast<float*>(smem + kMs);
-  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(smem + kBars);  // [2]
-  uint64_t* mma_bar = tma_bar + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tma_bar + 3);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars + 1);
 
   const gdn_prefill_args_t& a = p.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, half = warp >> 2;
   const int bh = blockIdx.x;
   const int b = bh / a.Hv, h = bh % a.Hv, hq = h / p.group;
   const int T = a.T;
+  const int nchunks = p.nchunks;
 
   if (warp == 0) tc::tmem_alloc(tmem_holder, kTmCols);
   if (tid == 0) {
-    mbar_init(&tma_bar[0], 1);
-    mbar_init(&tma_bar[1], 1);
-    mbar_init(mma_bar, 1);
+    mbar_init(&bars[kBarKQV], 1);
+    mbar_init(&bars[kBarKQV + 1], 1);
+    mbar_init(&bars[kBarIMma], 1);
+    mbar_init(&bars[kBarReady], kIntraThreads);
+    mbar_init(&bars[kBarReady + 1], kIntraThreads);
+    mbar_init(&bars[kBarX], 1);
+    mbar_init(&bars[kBarZ], 1);
+    mbar_init(&bars[kBarS2], 1);
+    mbar_init(&bars[kBarSlotFree], 1);
+    mbar_init(&bars[kBarSlotFree + 1], 1);
+    *abort_flag = 0;
     fence_mbar_init();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+  const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
   constexpr uint32_t kIdKQ = tc::idesc_f16(128, 64, false, false, BF16);
   constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, BF16);
-  constexpr uint32_t kIdX = tc::idesc_f16(128, 64, false, true, BF16);
+  constexpr uint32_t kIdXneg = tc::idesc_f16(128, 64, false, true, BF16, true);
   constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, BF16);
 
-  // ---- master state: thread owns S[k][dv] for k in [k0, k0 + 64)
-  const int dv = quarter * 32 + lane;
-  const int k0 = half * 64;
-  const size_t state_off = static_cast<size_t>(bh) * kD * kD;
-  float S[64];
-#pragma unroll
-  for (int j = 0; j < 64; ++j)
-    S[j] = a.initial_state ? a.initial_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] : 0.f;
-#pragma unroll
-  for (int cc = 0; cc < 8; ++cc) {
-    tc::sts128(sb + kST + half * kSTBlock + tc::sw128_offset(dv, cc),
-               tc::pack2<BF16>(S[8 * cc + 0], S[8 * cc + 1]), tc::pack2<BF16>(S[8 * cc + 2], S[8 * cc + 3]),
-               tc::pack2<BF16>(S[8 * cc + 4], S[8 * cc + 5]), tc::pack2<BF16>(S[8 * cc + 6], S[8 * cc + 7]));
-  }
-  tc::fence_proxy_async();
-
-  auto issue_tma = [&](int chunk) {
-    const int t0 = chunk * kC, buf = chunk & 1;
-    uint64_t* bar = &tma_bar[buf];
+  auto issue_tma = [&](int n) {  // K, Q, V of chunk n into slot n & 1
+    const int slot = n & 1;
+    uint64_t* bar = &bars[kBarKQV + slot];
     mbar_arrive_expect_tx(bar, 6 * 8192);
+    const int t0 = n * kC;
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
-      unsigned char* kq = smem + kKQ + buf * kKQBuf + blk * kKQBlock;
+      unsigned char* kq = smem + kKQ + slot * kKQSlot + blk * kKQBlock;
       tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, bar);
       tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, bar);
-      tc::tma_load_4d(smem + kV + buf * kVBuf + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
+      tc::tma_load_4d(smem + kV + slot * kVSlot + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
     }
   };
-  if (tid == 0) issue_tma(0);
+  if (tid == kIntraThreads) {
+    issue_tma(0);
+    if (nchunks > 1) issue_tma(1);
+  }
 
-  // gates of the next chunk are prefetched one chunk ahead into registers
-  float g_next = 0.f, b_next = 0.f;
-  auto load_gates = [&](int chunk) {
-    const int t = chunk * kC + tid;
-    if (tid < kC && t < T) {
-      const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + h;
-      g_next = load_any(a.g, gi, a.g_dtype);
-      b_next = load_any(a.beta, gi, a.beta_dtype);
-    } else {
+  if (warp < 4) {
+    // ================================================================ intra
+    const int it = tid;  // 0..127
+    float g_next = 0.f, b_next = 0.f;
+    auto load_gates = [&](int chunk) {
+      const int t = chunk * kC + it;
       g_next = 0.f;
       b_next = 0.f;
-    }
-  };
-  load_gates(0);
-  uint32_t mma_phase = 0;
-  bool failed = false;
-
-#pragma unroll 1
-  for (int c = 0; c < p.nchunks; ++c) {
-    const int t0 = c * kC, buf = c & 1;
-    const uint32_t kq = sb + kKQ + buf * kKQBuf;
-    const uint32_t vt = sb + kV + buf * kVBuf;
-    if (tid < kC) {
-      sGraw[tid] = g_next;
-      sBeta[tid] = b_next;
-    }
-    if (!cta_wait(&tma_bar[buf], (c >> 1) & 1)) { failed = true; break; }
-    TRACE(c, 0);
-    if (tid == 0 && c + 1 < p.nchunks) issue_tma(c + 1);  // into the other buffer
-    if (c + 1 < p.nchunks) load_gates(c + 1);
-
-    // ---- MMA 1: [K;Q] K^T -> KQ ; S^T Q^T -> Z
-    if (tid == 0) {
-      tc::fence_after_sync();
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        tc::mma(tmem + kTmKQ, tc::kmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(kq, kKQBlock, s), kIdKQ,
-                s > 0);
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        tc::mma(tmem + kTmZ, tc::kmajor_desc(sb + kST, kSTBlock, s),
-                tc::kmajor_desc(kq + 8192, kKQBlock, s), kIdKQ, s > 0);
-      tc::commit(mma_bar);
-    }
-    // ---- in-chunk cumulative gate (warp 0): lane l owns tokens 2l, 2l+1
-    if (warp == 0) {
-      const float g0 = sGraw[2 * lane], g1 = sGraw[2 * lane + 1];
-      float run = g0 + g1;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float o = __shfl_up_sync(0xffffffffu, run, off);
-        if (lane >= off) run += o;
+      if (it < kC && t < T) {
+        const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + h;
+        g_next = load_any(a.g, gi, a.g_dtype);
+        b_next = load_any(a.beta, gi, a.beta_dtype);
       }
-      const float excl = run - (g0 + g1);
-      sG[2 * lane] = excl + g0;
-      sG[2 * lane + 1] = run;
-      sGam[2 * lane] = __expf(excl + g0);
-      sGam[2 * lane + 1] = __expf(run);
-    }
-    if (!cta_wait(mma_bar, mma_phase)) { failed = true; break; }
-    mma_phase ^= 1;
-    tc::fence_after_sync();
-    TRACE(c, 1);
-
-    // ---- A rows (K K^T, TMEM lanes 0-63) and P rows (Q K^T, lanes 64-127);
-    //      warps w and w+4 take columns [0,32) and [32,64)
-    {
-      const int i = (quarter & 1) * 32 + lane;
-      const float Gi = sG[i];
-      float r[32];
-      tc::tmem_ld16(tmem + lane_base + kTmKQ + half * 32, *reinterpret_cast<float(*)[16]>(r));
-      tc::tmem_ld16(tmem + lane_base + kTmKQ + half * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
-      tc::tmem_wait_ld();
-      if (quarter < 2) {
-        const float bi = sBeta[i];
+    };
+    load_gates(0);
+    uint32_t imma_phase = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c & 1;
+      float* sG = vec + (c % 3) * kVecSlot;
+      float* sGam = sG + 64;
+      float* sBeta = sG + 128;
+      float* sDecay = sG + 192;
+      const uint32_t kq = sb + kKQ + slot * kKQSlot;
+      const uint32_t vt = sb + kV + slot * kVSlot;
+      const uint32_t pt = sb + kP + slot * kPSlot;
+      const uint32_t tmu = tmem + kTmU + slot * 64;
+      float graw = g_next;
+      if (it < kC) sBeta[it] = b_next;
+      if (!group_wait(&bars[kBarKQV + slot], (c >> 1) & 1, kBarIntra, kIntraThreads)) break;
+      TRACE(c, 0);
+      if (it == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          tc::mma(tmem + kTmKQ, tc::kmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(kq, kKQBlock, s),
+                  kIdKQ, s > 0);
+        tc::commit(&bars[kBarIMma]);
+      }
+      if (c + 1 < nchunks) load_gates(c + 1);
+      // in-chunk cumulative log gate: threads 0..63 publish the raw gates, then
+      // warp 0 scans them (lane l owns tokens 2l, 2l+1)
+      if (it < kC) sG[it] = graw;
+      tc::group_sync(kBarIntra, kIntraThreads);
+      if (warp == 0) {
+        const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
+        float run = g0 + g1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float o = __shfl_up_sync(0xffffffffu, run, off);
+          if (lane >= off) run += o;
+        }
+        const float excl = run - (g0 + g1);
+        const float GC = __shfl_sync(0xffffffffu, run, 31);
+        __syncwarp();
+        sG[2 * lane] = excl + g0;
+        sG[2 * lane + 1] = run;
+        sGam[2 * lane] = __expf(excl + g0);
+        sGam[2 * lane + 1] = __expf(run);
+        sDecay[2 * lane] = __expf(GC - (excl + g0));  // exp(G_C - G_j): V'' row scale
+        sDecay[2 * lane + 1] = __expf(GC - run);
+      }
+      // P and U of this slot were last used by chunk c-2: wait until it is done
+      if (c >= 2 && !group_wait(&bars[kBarSlotFree + slot], ((c - 2) >> 1) & 1, kBarIntra, kIntraThreads))
+        break;
+      if (!group_wait(&bars[kBarIMma], imma_phase, kBarIntra, kIntraThreads)) break;
+      imma_phase ^= 1;
+      tc::fence_after_sync();
+      TRACE(c, 1);
+      {  // A rows (TMEM lanes 0-63) and P rows (lanes 64-127), 64 columns each
+        const int q = warp;
+        const int i = (q & 1) * 32 + lane;
+        float r[64];
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb)
+          tc::tmem_ld16(tmem + lane_base + kTmKQ + cb * 16, *reinterpret_cast<float(*)[16]>(r + cb * 16));
+        tc::tmem_wait_ld();
+        TRACE(c, 12);
+        const float Gi = sG[i];
+        if (q < 2) {
+          const float bi = sBeta[i];
+#pragma unroll
+          for (int j4 = 0; j4 < 64; j4 += 4) {
+            float4 v;
+            float* pv = reinterpret_cast<float*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = j4 + e;
+              pv[e] = (j < i) ? bi * __expf(Gi - sG[j]) * r[j] : 0.f;
+            }
+            *reinterpret_cast<float4*>(AT + i * kLd + j4) = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) r[j] = (j <= i) ? r[j] * __expf(Gi - sG[j]) : 0.f;
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) store_row16<BF16>(pt, i, cb * 2, r + cb * 16);
+        }
+      }
+      TRACE(c, 13);
+      tc::fence_before_sync();
+      tc::group_sync(kBarIntra, kIntraThreads);
+      TRACE(c, 2);
+      solve_unit_lower(AT, Ms, warp, lane);
+      TRACE(c, 3);
+      {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 32 columns
+        const int i = it >> 1, jh = it & 1;
+        float tw[32], tu[32];
 #pragma unroll
         for (int j4 = 0; j4 < 32; j4 += 4) {
-          float4 v;
-          float* pv = reinterpret_cast<float*>(&v);
+          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jh * 32 + j4);
+          const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = half * 32 + j4 + e;
-            pv[e] = (j < i) ? bi * __expf(Gi - sG[j]) * r[j4 + e] : 0.f;
+            const int j = jh * 32 + j4 + e;
+            const float t = (j <= i) ? tv[e] : 0.f;
+            tu[j4 + e] = t * sBeta[j];
+            tw[j4 + e] = tu[j4 + e] * sGam[j];
           }
-          *reinterpret_cast<float4*>(Af + i * kLd + half * 32 + j4) = v;
         }
-      } else {
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = half * 32 + jj;
-          r[jj] = (j <= i) ? r[jj] * __expf(Gi - sG[j]) : 0.f;
-        }
-        store_row16<BF16>(sb + kP, i, half * 4, r);
-        store_row16<BF16>(sb + kP, i, half * 4 + 2, r + 16);
+        store_row16<BF16>(sb + kTw, i, jh * 4, tw);
+        store_row16<BF16>(sb + kTw, i, jh * 4 + 2, tw + 16);
+        store_row16<BF16>(sb + kTu, i, jh * 4, tu);
+        store_row16<BF16>(sb + kTu, i, jh * 4 + 2, tu + 16);
       }
-    }
-    __syncthreads();
-    TRACE(c, 2);
-    solve_unit_lower(Af, Tf, Ms, tid);
-    TRACE(c, 3);
-    {
-      const int i = tid >> 2, jq = tid & 3;
-      float tw[16], tu[16];
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::group_sync(kBarIntra, kIntraThreads);
+      TRACE(c, 4);
+      if (it == 0) {  // W^T = K^T T_w^T (reuses the KQ columns), U^T = V^T T_u^T
+        tc::fence_after_sync();
 #pragma unroll
-      for (int j4 = 0; j4 < 16; j4 += 4) {
-        const float4 t4 = *reinterpret_cast<const float4*>(Tf + i * kLd + jq * 16 + j4);
-        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmem + kTmKQ, tc::mnmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(sb + kTw, 0, s),
+                  kIdW, s > 0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = jq * 16 + j4 + e;
-          const float t = (j <= i) ? tv[e] : 0.f;
-          tu[j4 + e] = t * sBeta[j];
-          tw[j4 + e] = tu[j4 + e] * sGam[j];
-        }
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmu, tc::mnmajor_desc(vt, kVBlock, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+        tc::commit(&bars[kBarIMma]);
       }
-      store_row16<BF16>(sb + kTw, i, jq * 2, tw);
-      store_row16<BF16>(sb + kTu, i, jq * 2, tu);
-    }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    TRACE(c, 4);
-
-    // ---- MMA 2: W^T = K^T T_w^T ; U^T = V^T T_u^T
-    if (tid == 0) {
+      // the W^T tile was read by the previous chunk's V' MMA: wait for it
+      if (c >= 1 && !group_wait(&bars[kBarX], (c - 1) & 1, kBarIntra, kIntraThreads)) break;
+      if (!group_wait(&bars[kBarIMma], imma_phase, kBarIntra, kIntraThreads)) break;
+      imma_phase ^= 1;
       tc::fence_after_sync();
+      TRACE(c, 5);
+      {  // W^T -> bf16 tile, MN-major rows d_k = warp*32 + lane, 64 tokens
+        const int k = warp * 32 + lane;
+        float r[64];
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        tc::mma(tmem + kTmW, tc::mnmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(sb + kTw, 0, s), kIdW,
-                s > 0);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        tc::mma(tmem + kTmU, tc::mnmajor_desc(vt, kVBlock, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW,
-                s > 0);
-      tc::commit(mma_bar);
-    }
-    if (!cta_wait(mma_bar, mma_phase)) { failed = true; break; }
-    mma_phase ^= 1;
-    tc::fence_after_sync();
-    TRACE(c, 5);
-    {  // W^T -> bf16 tile, MN-major rows d_k = quarter*32 + lane, tokens [32 half, +32)
-      const int k = quarter * 32 + lane;
-      float r[32];
-      tc::tmem_ld16(tmem + lane_base + kTmW + half * 32, *reinterpret_cast<float(*)[16]>(r));
-      tc::tmem_ld16(tmem + lane_base + kTmW + half * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
-      tc::tmem_wait_ld();
-      store_row16<BF16>(sb + kWT, k, half * 4, r);
-      store_row16<BF16>(sb + kWT, k, half * 4 + 2, r + 16);
-    }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    TRACE(c, 6);
-
-    // ---- MMA 3: X^T = S^T W^T
-    if (tid == 0) {
-      tc::fence_after_sync();
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        tc::mma(tmem + kTmX, tc::kmajor_desc(sb + kST, kSTBlock, s), tc::mnmajor_desc(sb + kWT, 8192, s),
-                kIdX, s > 0);
-      tc::commit(mma_bar);
-    }
-    if (!cta_wait(mma_bar, mma_phase)) { failed = true; break; }
-    mma_phase ^= 1;
-    tc::fence_after_sync();
-    TRACE(c, 7);
-    {  // V' = U - X ; V'' = V' exp(G_C - G_j) split hi / lo
-      const float GC = sG[kC - 1];
-      float u[32], x[32];
-      tc::tmem_ld16(tmem + lane_base + kTmU + half * 32, *reinterpret_cast<float(*)[16]>(u));
-      tc::tmem_ld16(tmem + lane_base + kTmU + half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
-      tc::tmem_ld16(tmem + lane_base + kTmX + half * 32, *reinterpret_cast<float(*)[16]>(x));
-      tc::tmem_ld16(tmem + lane_base + kTmX + half * 32 + 16, *reinterpret_cast<float(*)[16]>(x + 16));
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        float vp[16], hi[16], lo[16];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = half * 32 + cb * 16 + jj;
-          vp[jj] = u[cb * 16 + jj] - x[cb * 16 + jj];
-          const float vd = vp[jj] * __expf(GC - sG[j]);
-          hi[jj] = tc::unpack_lo<BF16>(tc::pack2<BF16>(vd, 0.f));
-          lo[jj] = vd - hi[jj];
-        }
-        store_row16<BF16>(sb + kVP, dv, half * 4 + cb * 2, vp);
-        store_row16<BF16>(sb + kVH, dv, half * 4 + cb * 2, hi);
-        store_row16<BF16>(sb + kVL, dv, half * 4 + cb * 2, lo);
-      }
-    }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    TRACE(c, 8);
-
-    // ---- MMA 4: O_intra^T = V'^T P^T ; dS^T = V''hi^T K + V''lo^T K
-    if (tid == 0) {
-      tc::fence_after_sync();
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        tc::mma(tmem + kTmOI, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(sb + kP, 0, s), kIdKQ,
-                s > 0);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVH, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
-                s > 0);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVL, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
-                true);
-      tc::commit(mma_bar);
-    }
-    if (!cta_wait(mma_bar, mma_phase)) { failed = true; break; }
-    mma_phase ^= 1;
-    tc::fence_after_sync();
-    TRACE(c, 9);
-
-    {  // state update and bf16 copy for the next chunk
-      const float gC = sGam[kC - 1];
-#pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        float r[32];
-        tc::tmem_ld16(tmem + lane_base + kTmDS + half * 64 + hb * 32, *reinterpret_cast<float(*)[16]>(r));
-        tc::tmem_ld16(tmem + lane_base + kTmDS + half * 64 + hb * 32 + 16,
-                      *reinterpret_cast<float(*)[16]>(r + 16));
+        for (int cb = 0; cb < 4; ++cb)
+          tc::tmem_ld16(tmem + lane_base + kTmKQ + cb * 16, *reinterpret_cast<float(*)[16]>(r + cb * 16));
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) S[hb * 32 + jj] = fmaf(gC, S[hb * 32 + jj], r[jj]);
+        for (int cb = 0; cb < 4; ++cb) store_row16<BF16>(sb + kWT, k, cb * 2, r + cb * 16);
       }
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        tc::sts128(sb + kST + half * kSTBlock + tc::sw128_offset(dv, cc),
-                   tc::pack2<BF16>(S[8 * cc + 0], S[8 * cc + 1]), tc::pack2<BF16>(S[8 * cc + 2], S[8 * cc + 3]),
-                   tc::pack2<BF16>(S[8 * cc + 4], S[8 * cc + 5]), tc::pack2<BF16>(S[8 * cc + 6], S[8 * cc + 7]));
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      mbar_arrive(&bars[kBarReady + slot]);
+      TRACE(c, 6);
     }
-    {  // outputs o[t0 + i][dv] = scale (gamma_i Z[dv][i] + O_intra[dv][i])
-      IO* o = static_cast<IO*>(a.o);
+  } else {
+    // ================================================================ state
+    const int st = tid - kIntraThreads;  // 0..255
+    const int quarter = warp & 3, half = (warp - 4) >> 2;
+    const int dv = quarter * 32 + lane;
+    const int k0 = half * 64;
+    const size_t state_off = static_cast<size_t>(bh) * kD * kD;
+    IO* o = static_cast<IO*>(a.o);
+    float S[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      S[j] = a.initial_state ? a.initial_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] : 0.f;
+    auto write_st = [&]() {  // bf16 S^T into TMEM: lane dv, packed d_k pairs
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        uint32_t u[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) u[e] = pack_bits<BF16>(S[cb * 32 + 2 * e], S[cb * 32 + 2 * e + 1]);
+        tc::tmem_st16(tmem + lane_base + kTmST + half * 32 + cb * 16, u);
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+    };
+    // outputs o[t0 + i][dv] = scale (gamma_i Z[dv][i] + O_intra[dv][i]): staged
+    // as a [64][128] tile in the V''hi buffer (free between the previous
+    // chunk's last MMA and this chunk's V'' epilogue), then written with
+    // coalesced 16-byte stores
+    auto outputs = [&](int c) {
+      const float* sGam = vec + (c % 3) * kVecSlot + 64;
+      IO* stage = reinterpret_cast<IO*>(smem + kVH);
       float z[32], oi[32];
       tc::tmem_ld16(tmem + lane_base + kTmZ + half * 32, *reinterpret_cast<float(*)[16]>(z));
       tc::tmem_ld16(tmem + lane_base + kTmZ + half * 32 + 16, *reinterpret_cast<float(*)[16]>(z + 16));
@@ -556,25 +533,140 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const int i = half * 32 + jj;
-        const int t = t0 + i;
-        if (t < T)
-          o[((static_cast<int64_t>(b) * T + t) * a.Hv + h) * kD + dv] =
-              from_f32<IO>(a.scale * fmaf(sGam[i], z[jj], oi[jj]));
+        stage[i * kD + dv] = from_f32<IO>(a.scale * fmaf(sGam[i], z[jj], oi[jj]));
+      }
+      tc::fence_before_sync();
+      tc::group_sync(kBarState, kStateThreads);
+      const int t0 = c * kC;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {  // 64 rows x 256 B = 1024 16-byte pieces
+        const int piece = r * kStateThreads + st;
+        const int i = piece >> 4, col = (piece & 15) * 8;
+        if (t0 + i < T) {
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + i * kD + col);
+          *reinterpret_cast<uint4*>(o + ((static_cast<int64_t>(b) * T + t0 + i) * a.Hv + h) * kD + col) = v;
+        }
+      }
+    };
+    write_st();
+    tc::group_sync(kBarState, kStateThreads);
+    uint32_t x_phase = 0, z_phase = 0, s2_phase = 0;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c & 1;
+      const float* sG = vec + (c % 3) * kVecSlot;
+      const float* sGam = sG + 64;
+      const float* sDecay = sG + 192;
+      const uint32_t kq = sb + kKQ + slot * kKQSlot;
+      const uint32_t pt = sb + kP + slot * kPSlot;
+      const uint32_t tmu = tmem + kTmU + slot * 64;
+      if (!group_wait(&bars[kBarReady + slot], (c >> 1) & 1, kBarState, kStateThreads)) { ok = false; break; }
+      TRACE(c, 7);
+      if (st == 0) {  // V'^T = U^T - S^T W^T  (A = S^T from TMEM, negated)
+        tc::fence_after_sync();
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          tc::mma_tmem_a(tmu, tmem + kTmST + s * 8, tc::mnmajor_desc(sb + kWT, 8192, s), kIdXneg, true);
+        tc::commit(&bars[kBarX]);
+      }
+      if (c >= 1) {  // outputs of the previous chunk overlap the V' MMA
+        if (!group_wait(&bars[kBarZ], z_phase, kBarState, kStateThreads)) { ok = false; break; }
+        z_phase ^= 1;
+        tc::fence_after_sync();
+        outputs(c - 1);
+      }
+      tc::group_sync(kBarState, kStateThreads);
+      if (st == 0) {  // Z^T = S^T Q^T
+        tc::fence_after_sync();
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          tc::mma_tmem_a(tmem + kTmZ, tmem + kTmST + s * 8, tc::kmajor_desc(kq + 8192, kKQBlock, s),
+                         kIdKQ, s > 0);
+        tc::commit(&bars[kBarZ]);
+      }
+      if (!group_wait(&bars[kBarX], x_phase, kBarState, kStateThreads)) { ok = false; break; }
+      x_phase ^= 1;
+      tc::fence_after_sync();
+      TRACE(c, 8);
+      {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> hi / lo tiles
+        float u[32];
+        tc::tmem_ld16(tmu + lane_base + half * 32, *reinterpret_cast<float(*)[16]>(u));
+        tc::tmem_ld16(tmu + lane_base + half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          float hi[16], lo[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = half * 32 + cb * 16 + jj;
+            const float vd = u[cb * 16 + jj] * sDecay[j];
+            hi[jj] = tc::unpack_lo<BF16>(tc::pack2<BF16>(vd, 0.f));
+            lo[jj] = vd - hi[jj];
+          }
+          store_row16<BF16>(sb + kVP, dv, half * 4 + cb * 2, u + cb * 16);
+          store_row16<BF16>(sb + kVH, dv, half * 4 + cb * 2, hi);
+          store_row16<BF16>(sb + kVL, dv, half * 4 + cb * 2, lo);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::group_sync(kBarState, kStateThreads);
+      TRACE(c, 9);
+      if (st == 0) {  // O_intra^T = V'^T P^T ; dS^T = V''hi^T K + V''lo^T K
+        tc::fence_after_sync();
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmem + kTmOI, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(pt, 0, s), kIdKQ, s > 0);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVH, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
+                  s > 0);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVL, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
+                  true);
+        tc::commit(&bars[kBarS2]);
+        tc::commit(&bars[kBarSlotFree + slot]);
+      }
+      if (!group_wait(&bars[kBarS2], s2_phase, kBarState, kStateThreads)) { ok = false; break; }
+      s2_phase ^= 1;
+      tc::fence_after_sync();
+      if (st == 0 && c + 2 < nchunks) issue_tma(c + 2);  // this slot's MMAs are done
+      TRACE(c, 10);
+      {  // S <- gamma_C S + dS ; bf16 S^T back into TMEM for the next chunk
+        const float gC = sGam[kC - 1];
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          float r[32];
+          tc::tmem_ld16(tmem + lane_base + kTmDS + half * 64 + hb * 32, *reinterpret_cast<float(*)[16]>(r));
+          tc::tmem_ld16(tmem + lane_base + kTmDS + half * 64 + hb * 32 + 16,
+                        *reinterpret_cast<float(*)[16]>(r + 16));
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) S[hb * 32 + jj] = fmaf(gC, S[hb * 32 + jj], r[jj]);
+        }
+        write_st();
+      }
+      tc::group_sync(kBarState, kStateThreads);
+      TRACE(c, 11);
+    }
+    if (ok && nchunks > 0) {
+      if (group_wait(&bars[kBarZ], z_phase, kBarState, kStateThreads)) {
+        tc::fence_after_sync();
+        outputs(nchunks - 1);
+#pragma unroll
+        for (int j = 0; j < 64; ++j)
+          a.final_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] = S[j];
+      } else {
+        ok = false;
       }
     }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    TRACE(c, 10);
+    if (!ok && st == 0) {
+      report(a.status, GDN_DEVERR_MMA_TIMEOUT);
+      *abort_flag = 1;
+    }
   }
 
-  if (failed) {
-    if (tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 64; ++j)
-      a.final_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] = S[j];
-  }
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);

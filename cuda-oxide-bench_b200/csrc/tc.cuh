@@ -47,8 +47,10 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, uint32_t mnblock
 }
 
 // Instruction descriptor: 16-bit inputs (bf16 if bf16 else f16), fp32 accumulate.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn, bool bf16) {
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn, bool bf16,
+                                                 bool a_neg = false) {
   return (1u << 4)                                   // D format f32
+         | ((a_neg ? 1u : 0u) << 13)                 // negate A
          | ((bf16 ? 1u : 0u) << 7)                   // A format
          | ((bf16 ? 1u : 0u) << 10)                  // B format
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
@@ -116,6 +118,37 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns from registers (thread i -> lane
+// quarter*32 + i).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&u)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]),
+      "r"(u[8]), "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// MMA with the A operand read from TMEM (M rows = lanes, 16-bit elements
+// packed two per 32-bit column, lower element in the low half).
+__device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                           uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(static_cast<uint32_t>(accumulate))
+      : "memory");
+}
+
+// Named barrier over `count` threads (a thread group inside the CTA).
+__device__ __forceinline__ void group_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 4-D tiled load (no multicast) into a 128B-swizzled tile.  c0 * element
 // size must be a multiple of 16 bytes.
@@ -126,6 +159,20 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       "{%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
+}
+
+// bf16 round-to-nearest-even on the integer pipe: returns the rounded bit
+// pattern with the bf16 value in the upper 16 bits (lower 16 bits garbage).
+// Finite inputs only (the kernels never feed NaN); overflow rounds to inf.
+// Keeps the conversion off the transcendental/conversion (XU) pipe, which
+// the prefill epilogues would otherwise saturate.
+__device__ __forceinline__ uint32_t bf16_rne_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return u + 0x7FFFu + ((u >> 16) & 1u);
+}
+// The float value of x rounded to bf16.
+__device__ __forceinline__ float bf16_round(float x) {
+  return __uint_as_float(bf16_rne_bits(x) & 0xFFFF0000u);
 }
 
 // packs two floats into a bf16x2 / f16x2 word (low half = first)
