@@ -225,7 +225,8 @@ def run_gpu(args, world, rank, local):
     # decode of step i + 1; step i + 2 waits for it before reusing the buffer
     outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     out = outs[0]
-    res = args.sm_reserve if world > 1 else 0
+    res = args.sm_reserve if args.sm_reserve >= 0 else min(48, 8 * world if world > 2 else 16)
+    res = res if world > 1 else 0
     steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
     steps2 = [pkg.DecodeStep(*t, state, out=outs[1], sm_reserve=res) for t in toks]
     gbufs = [torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)] \
@@ -260,29 +261,67 @@ def run_gpu(args, world, rank, local):
     settle(args.warmup)
     settle(args.warmup + 1)
     pkg.check_device_status(dev)
+    use_graph = world > 1 and not args.no_graph
+    n_kev = min(args.steps, 200) if use_graph else args.steps
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+           for _ in range(n_kev)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def eager_steps(n, record):
+        for i in range(n):
+            settle(i)
+            if record:
+                kev[i][0].record(stream)
+            launch(i)
+            if record:
+                kev[i][1].record(stream)
+            gather(i)
+            if args.no_overlap:
+                settle(i)
+        settle(n)
+        settle(n + 1)
+
+    graph = None
+    if use_graph:
+        # N > 1: steps are short (the state per GPU shrinks as 1/N), so the host
+        # loop of one library launch + one NCCL call per step would bound the
+        # rate.  Capture G steps (decode + overlapped all-gather) in a CUDA
+        # graph and replay it; kernel durations come from an eager pass.
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        eager_steps(n_kev, True)
+        torch.cuda.synchronize(dev)
+        kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / n_kev, world, dev)
+        G = 10
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                eager_steps(G, False)
+        torch.cuda.current_stream(dev).wait_stream(cap)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        replays = max(1, args.steps // G)
+        timed_steps = replays * G
+    else:
+        timed_steps = args.steps
     barrier(world)
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for i in range(args.steps):
-            settle(i)
-            kev[i][0].record(stream)
-            launch(i)
-            kev[i][1].record(stream)
-            gather(i)
-            if args.no_overlap:
-                settle(i)
-        settle(args.steps)
-        settle(args.steps + 1)
+        if graph is not None:
+            for _ in range(replays):
+                graph.replay()
+        else:
+            eager_steps(args.steps, True)
         e1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
     pkg.check_device_status(dev)
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
-    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps, world, dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / timed_steps, world, dev)
+    if graph is None:
+        kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps, world, dev)
     total_bytes = inputs.gdn_decode_bytes(B, HQK, HV, D, D)
     value = total_bytes / (ms * 1e-3) / 1e9
     local_bytes = inputs.gdn_decode_bytes(B, hq, hv, D, D)
@@ -338,7 +377,7 @@ def run_gpu(args, world, rank, local):
     traffic = profiled_traffic(f"gdn_decode_B{B}")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "steps": timed_steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (BASELINE distributions, seed 0)",
         "config": {"workload": "GDN decode (BASELINE configs[1], B=1024; config 4 at N>1)",
@@ -356,7 +395,8 @@ def run_gpu(args, world, rank, local):
                      "algorithmic_bytes_per_launch": local_bytes},
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps,
+        "gpu_launches": timed_steps,
+        "cuda_graph": graph is not None,
         "allgather_overlapped": world > 1 and not args.no_overlap,
         "sm_reserve": res,
         "clocks": clk.summary(),
@@ -498,8 +538,11 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--sm-reserve", type=int, default=16,
-                    help="SMs the decode leaves to the overlapped all-gather (N>1)")
+    ap.add_argument("--sm-reserve", type=int, default=-1,
+                    help="SMs the decode leaves to the overlapped all-gather (N>1); default "
+                         "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="N>1: run each step's all-gather after its decode, not overlapped")
     ap.add_argument("--workload", default="decode", choices=("decode", "prefill"),
