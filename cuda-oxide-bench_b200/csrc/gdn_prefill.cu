@@ -26,11 +26,11 @@
 // is split into bf16 hi + lo halves (two MMAs), and K enters the state update
 // unscaled, so the state accumulates with ~16 mantissa bits per term.
 //
-// One CTA per (batch, value head), 12 warps in two roles that run
+// One CTA per (batch, value head), 16 warps in two roles that run
 // concurrently, one chunk apart:
-//   intra (warps 0-3):   KQ MMA, A and P rows, T = (I+A)^-1, W/U MMAs, W^T tile
+//   intra (warps 0-7):   KQ MMA, A and P rows, T = (I+A)^-1, W/U MMAs, W^T tile
 //                        for chunk c+1 ...
-//   state (warps 4-11):  ... while the state chain of chunk c runs: V' = U - W S,
+//   state (warps 8-15):  ... while the state chain of chunk c runs: V' = U - W S,
 //                        V'/V'' tiles, O_intra/dS MMAs, state update, outputs.
 // K/Q/V are double-buffered; the state warps' MMA thread refills a slot with
 // chunk c+2 by TMA as soon as chunk c's last MMA on it has completed.
@@ -54,7 +54,7 @@ namespace prefill {
 __device__ unsigned long long g_trace[64 * 16];
 #define TRACE(c, ph)                                                                           \
   do {                                                                                         \
-    if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x == 0 || threadIdx.x == 128))              \
+    if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x == 0 || threadIdx.x == kIntraThreads))              \
       g_trace[(c) * 16 + (ph)] = global_timer_ns();                                            \
   } while (0)
 #else
@@ -65,7 +65,7 @@ __device__ unsigned long long g_trace[64 * 16];
 
 constexpr int kC = 64;     // chunk length
 constexpr int kD = 128;    // d_k = d_v
-constexpr int kIntraThreads = 128;
+constexpr int kIntraThreads = 256;
 constexpr int kStateThreads = 256;
 constexpr int kThreads = kIntraThreads + kStateThreads;
 constexpr int kBarIntra = 1, kBarState = 2;  // named barrier ids
@@ -191,14 +191,14 @@ __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], 
 }
 
 // In place: AT holds strictly-lower A (64 x 64 fp32, stride kLd, zeros on and
-// above the diagonal) and is overwritten with T = (I + A)^-1.  Run by the 4
-// intra warps (128 threads).  Steps: the four 16 x 16 diagonal blocks D_r by
+// above the diagonal) and is overwritten with T = (I + A)^-1.  Run by the
+// intra warps (warps 0-3 compute; the others only join the group barriers).  Steps: the four 16 x 16 diagonal blocks D_r by
 // forward substitution (one warp each, one lane per column, fp32); T_10 =
 // -D_1 A_10 D_0 and T_32 = -D_3 A_32 D_2; then the lower-left quadrant
 // -T_bot A_bl T_top through Y = A_bl T_top.  Each block of A is last read
 // before the block of T that replaces it is written.
 __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, int lane) {
-  {
+  if (warp < 4) {
     const int bb = warp * 16, c = lane & 15;
     float t[16];
 #pragma unroll
@@ -236,7 +236,7 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
     block_store(AT + 16 * r * kLd + 16 * c, acc2, -1.f, lane);
   }
   tc::group_sync(kBarIntra, kIntraThreads);
-  {  // Y_rc = sum_k A_rk T_kc over the top blocks, warp (r-2)*2 + c
+  if (warp < 4) {  // Y_rc = sum_k A_rk T_kc over the top blocks, warp (r-2)*2 + c
     const int r = 2 + (warp >> 1), c = warp & 1;
     float acc[2][4] = {};
     if (c == 0) {
@@ -248,7 +248,7 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
     block_store(M + (r - 2) * 16 * kLd + 16 * c, acc, 1.f, lane);
   }
   tc::group_sync(kBarIntra, kIntraThreads);
-  {
+  if (warp < 4) {
     const int r = 2 + (warp >> 1), c = warp & 1;
     float acc[2][4] = {};
     if (r == 2) {
@@ -334,9 +334,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (nchunks > 1) issue_tma(1);
   }
 
-  if (warp < 4) {
+  if (warp < kIntraThreads / 32) {
     // ================================================================ intra
-    const int it = tid;  // 0..127
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    const int it = tid;  // 0..255
+    const int quarter = warp & 3, ih = warp >> 2;
     float g_next = 0.f, b_next = 0.f;
     auto load_gates = [&](int chunk) {
       const int t = chunk * kC + it;
@@ -402,34 +404,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       imma_phase ^= 1;
       tc::fence_after_sync();
       TRACE(c, 1);
-      {  // A rows (TMEM lanes 0-63) and P rows (lanes 64-127), 64 columns each
-        const int q = warp;
-        const int i = (q & 1) * 32 + lane;
-        float r[64];
+      {  // A rows (TMEM lanes 0-63) and P rows (lanes 64-127); warps w and w+4
+         // take columns [0, 32) and [32, 64)
+        const int i = (quarter & 1) * 32 + lane;
+        float r[32];
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
-          tc::tmem_ld16(tmem + lane_base + kTmKQ + cb * 16, *reinterpret_cast<float(*)[16]>(r + cb * 16));
+        for (int cb = 0; cb < 2; ++cb)
+          tc::tmem_ld16(tmem + lane_base + kTmKQ + ih * 32 + cb * 16,
+                        *reinterpret_cast<float(*)[16]>(r + cb * 16));
         tc::tmem_wait_ld();
         TRACE(c, 12);
         const float Gi = sG[i];
-        if (q < 2) {
+        if (quarter < 2) {
           const float bi = sBeta[i];
 #pragma unroll
-          for (int j4 = 0; j4 < 64; j4 += 4) {
+          for (int j4 = 0; j4 < 32; j4 += 4) {
             float4 v;
             float* pv = reinterpret_cast<float*>(&v);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int j = j4 + e;
-              pv[e] = (j < i) ? bi * __expf(Gi - sG[j]) * r[j] : 0.f;
+              const int j = ih * 32 + j4 + e;
+              pv[e] = (j < i) ? bi * __expf(Gi - sG[j]) * r[j4 + e] : 0.f;
             }
-            *reinterpret_cast<float4*>(AT + i * kLd + j4) = v;
+            *reinterpret_cast<float4*>(AT + i * kLd + ih * 32 + j4) = v;
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) r[j] = (j <= i) ? r[j] * __expf(Gi - sG[j]) : 0.f;
-#pragma unroll
-          for (int cb = 0; cb < 4; ++cb) store_row16<BF16>(pt, i, cb * 2, r + cb * 16);
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = ih * 32 + jj;
+            r[jj] = (j <= i) ? r[jj] * __expf(Gi - sG[j]) : 0.f;
+          }
+          store_row16<BF16>(pt, i, ih * 4, r);
+          store_row16<BF16>(pt, i, ih * 4 + 2, r + 16);
         }
       }
       TRACE(c, 13);
@@ -438,25 +444,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       TRACE(c, 2);
       solve_unit_lower(AT, Ms, warp, lane);
       TRACE(c, 3);
-      {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 32 columns
-        const int i = it >> 1, jh = it & 1;
-        float tw[32], tu[32];
+      {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 16 columns
+        const int i = it >> 2, jq = it & 3;
+        float tw[16], tu[16];
 #pragma unroll
-        for (int j4 = 0; j4 < 32; j4 += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jh * 32 + j4);
+        for (int j4 = 0; j4 < 16; j4 += 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jq * 16 + j4);
           const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = jh * 32 + j4 + e;
+            const int j = jq * 16 + j4 + e;
             const float t = (j <= i) ? tv[e] : 0.f;
             tu[j4 + e] = t * sBeta[j];
             tw[j4 + e] = tu[j4 + e] * sGam[j];
           }
         }
-        store_row16<BF16>(sb + kTw, i, jh * 4, tw);
-        store_row16<BF16>(sb + kTw, i, jh * 4 + 2, tw + 16);
-        store_row16<BF16>(sb + kTu, i, jh * 4, tu);
-        store_row16<BF16>(sb + kTu, i, jh * 4 + 2, tu + 16);
+        store_row16<BF16>(sb + kTw, i, jq * 2, tw);
+        store_row16<BF16>(sb + kTu, i, jq * 2, tu);
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
@@ -479,15 +483,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       imma_phase ^= 1;
       tc::fence_after_sync();
       TRACE(c, 5);
-      {  // W^T -> bf16 tile, MN-major rows d_k = warp*32 + lane, 64 tokens
-        const int k = warp * 32 + lane;
-        float r[64];
+      {  // W^T -> bf16 tile, MN-major rows d_k = quarter*32 + lane, tokens [32 ih, +32)
+        const int k = quarter * 32 + lane;
+        float r[32];
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
-          tc::tmem_ld16(tmem + lane_base + kTmKQ + cb * 16, *reinterpret_cast<float(*)[16]>(r + cb * 16));
+        for (int cb = 0; cb < 2; ++cb)
+          tc::tmem_ld16(tmem + lane_base + kTmKQ + ih * 32 + cb * 16,
+                        *reinterpret_cast<float(*)[16]>(r + cb * 16));
         tc::tmem_wait_ld();
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) store_row16<BF16>(sb + kWT, k, cb * 2, r + cb * 16);
+        store_row16<BF16>(sb + kWT, k, ih * 4, r);
+        store_row16<BF16>(sb + kWT, k, ih * 4 + 2, r + 16);
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
@@ -496,8 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ================================================================ state
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 168;" ::: "memory");
     const int st = tid - kIntraThreads;  // 0..255
-    const int quarter = warp & 3, half = (warp - 4) >> 2;
+    const int quarter = warp & 3, half = (warp - kIntraThreads / 32) >> 2;
     const int dv = quarter * 32 + lane;
     const int k0 = half * 64;
     const size_t state_off = static_cast<size_t>(bh) * kD * kD;
