@@ -14,6 +14,7 @@ namespace gdn {
 struct DeviceInfo {
   int sm_count = 0;
   int smem_optin = 0;  // max dynamic shared memory per block (opt-in)
+  int smem_per_sm = 0; // shared memory per SM
   int cc_major = 0, cc_minor = 0;
 };
 

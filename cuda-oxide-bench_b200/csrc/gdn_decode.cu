@@ -61,6 +61,10 @@ struct DecodeTraits {
   static constexpr int kRowGroups = kConsumers / kColGroups;  // thread rows
   static constexpr int kRows = DK / kRowGroups;               // rows per thread
   static constexpr int kMaxStages = 8;
+  // Narrow (32-column) slabs come with small batches, where a CTA walks a few
+  // slabs back to back and each slab's reduction latency is exposed: those
+  // variants run two CTAs per SM (fewer registers, half the smem ring each).
+  static constexpr int kCtasPerSm = BV == 32 ? 2 : 1;
   static constexpr uint32_t kSlabBytes = DK * BV * 4;
   static constexpr uint32_t kQKBytes = DK * 2;
   static constexpr uint32_t kVBytes = BV * 2;
@@ -75,7 +79,8 @@ struct DecodeTraits {
 };
 
 template <int DK, int BV, typename IO, bool KDA>
-__global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads, 1)
+__global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
+                                  DecodeTraits<DK, BV, KDA>::kCtasPerSm)
     decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap state_map) {
   using Tr = DecodeTraits<DK, BV, KDA>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -308,8 +313,10 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
+  const int smem_budget = Tr::kCtasPerSm == 1 ? di.smem_optin
+                                              : di.smem_per_sm / Tr::kCtasPerSm - 1024;
   int stages =
-      (di.smem_optin - static_cast<int>(Tr::kHeaderBytes) - 128) / static_cast<int>(Tr::kStageBytes);
+      (smem_budget - static_cast<int>(Tr::kHeaderBytes) - 128) / static_cast<int>(Tr::kStageBytes);
   if (stages > Tr::kMaxStages) stages = Tr::kMaxStages;
   if (stages < 2) return GDN_ERR_SHAPE;
   const int smem = Tr::kHeaderBytes + 128 + stages * Tr::kStageBytes;
@@ -332,7 +339,7 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
     rc = fp32_tensor_map_2d(&map, a.state_in, static_cast<uint64_t>(a.B) * a.Hv * DK, a.dv, DK, BV);
     if (rc) return rc;
   }
-  int ctas = di.sm_count - (a.sm_reserve > 0 ? a.sm_reserve : 0);
+  int ctas = (di.sm_count - (a.sm_reserve > 0 ? a.sm_reserve : 0)) * Tr::kCtasPerSm;
   if (ctas < 1) ctas = 1;
   const int64_t grid64 = p.total_slabs < ctas ? p.total_slabs : ctas;
   kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p, map);
