@@ -225,8 +225,9 @@ def run_gpu(args, world, rank, local):
     # decode of step i + 1; step i + 2 waits for it before reusing the buffer
     outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     out = outs[0]
+    ce = world > 1 and args.gather == "ce"
     res = args.sm_reserve if args.sm_reserve >= 0 else min(48, 8 * world if world > 2 else 16)
-    res = res if world > 1 else 0
+    res = res if (world > 1 and not ce) else 0
     steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
     steps2 = [pkg.DecodeStep(*t, state, out=outs[1], sm_reserve=res) for t in toks]
     gbufs = [torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)] \
@@ -237,16 +238,47 @@ def run_gpu(args, world, rank, local):
     def launch(i):
         (steps if i % 2 == 0 else steps2)[i % pool]()
 
+    if ce:
+        # copy-engine all-gather (no SMs): push on a side stream after each
+        # decode; the decode of step i + 2 waits for step i's copies to leave
+        # its output buffer
+        pg = sharded.PeerGather(B * hv * D, torch.bfloat16, dev)
+        side = torch.cuda.Stream(dev)
+        ev_dec = [torch.cuda.Event() for _ in range(2)]
+        ev_out_free = [None, None]
+        gstep = [0]
+
     def gather(i):
-        if world > 1:
+        if world > 1 and ce:
+            gstep[0] += 1
+            ms_ = torch.cuda.current_stream(dev)
+            ev_dec[i % 2].record(ms_)
+            side.wait_event(ev_dec[i % 2])
+            pg.push(outs[i % 2], gstep[0], side)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            ev_out_free[i % 2] = ev
+            pg.wait(gstep[0], side)      # every rank's slice of this step has landed
+            pg.release(gstep[0], side)   # (the bench consumes nothing further)
+        elif world > 1:
             works[i % 2] = dist.all_gather_into_tensor(gbufs[i % 2].view(-1), outs[i % 2].view(-1),
                                                        async_op=True)
 
     def settle(i):
+        if ce:
+            ev = ev_out_free[i % 2]
+            if ev is not None:
+                torch.cuda.current_stream(dev).wait_event(ev)
+                ev_out_free[i % 2] = None
+            return
         w = works[i % 2]
         if w is not None:
             w.wait()
             works[i % 2] = None
+
+    def join():
+        if ce:
+            torch.cuda.current_stream(dev).wait_stream(side)
 
     def one_step(i):
         settle(i)
@@ -260,8 +292,9 @@ def run_gpu(args, world, rank, local):
         one_step(i)
     settle(args.warmup)
     settle(args.warmup + 1)
+    join()
     pkg.check_device_status(dev)
-    use_graph = world > 1 and not args.no_graph
+    use_graph = world > 1 and not args.no_graph and not ce
     n_kev = min(args.steps, 200) if use_graph else args.steps
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_kev)]
@@ -280,6 +313,7 @@ def run_gpu(args, world, rank, local):
                 settle(i)
         settle(n)
         settle(n + 1)
+        join()
 
     graph = None
     if use_graph:
@@ -383,7 +417,8 @@ def run_gpu(args, world, rank, local):
         "config": {"workload": "GDN decode (BASELINE configs[1], B=1024; config 4 at N>1)",
                    "global_batch": B, "Hqk": HQK, "Hv": HV, "d_k": D, "d_v": D,
                    "io_dtype": "bf16", "state": "fp32 in place",
-                   "parallelism": f"value-head shard x{world}" + (" + NCCL all-gather of o"
+                   "parallelism": f"value-head shard x{world}" + (
+                       (" + copy-engine all-gather of o" if ce else " + NCCL all-gather of o")
                                                                  if world > 1 else ""),
                    "l2": "inputs larger than L2 (4.3 GB state), no flush"},
         "tokens_per_s": round(B / (ms * 1e-3), 1),
@@ -398,6 +433,7 @@ def run_gpu(args, world, rank, local):
         "gpu_launches": timed_steps,
         "cuda_graph": graph is not None,
         "allgather_overlapped": world > 1 and not args.no_overlap,
+        "allgather": ("copy-engine push over NVLink (IPC)" if ce else "NCCL") if world > 1 else None,
         "sm_reserve": res,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
@@ -541,6 +577,8 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the decode leaves to the overlapped all-gather (N>1); default "
                          "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
+    ap.add_argument("--gather", default="ce", choices=("ce", "nccl"),
+                    help="N>1 output all-gather: copy engines over NVLink (ce) or NCCL")
     ap.add_argument("--no-graph", action="store_true",
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",

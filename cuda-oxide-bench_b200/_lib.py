@@ -36,7 +36,13 @@ EXPORTED = (
     "kda_decode_ref_launch",
     "gdn_prefill_workspace_size",
     "gdn_prefill_launch",
+    "gdn_ipc_handle",
+    "gdn_ipc_open",
+    "gdn_ipc_close",
+    "gdn_gather_push",
+    "gdn_gather_wait",
 )
+IPC_HANDLE_BYTES = 64
 
 
 class GDNError(RuntimeError):
@@ -119,6 +125,15 @@ def load(path: str | Path | None = None):
         L.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         L.gdn_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
         L.gdn_prefill_launch.restype = ctypes.c_int
+        L.gdn_ipc_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
+        L.gdn_ipc_open.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
+        L.gdn_ipc_close.argtypes = [vp]
+        L.gdn_gather_push.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp), ctypes.POINTER(vp),
+                                      i32, ctypes.c_uint32, vp]
+        L.gdn_gather_wait.argtypes = [vp, i32, ctypes.c_uint32, vp]
+        for fn in (L.gdn_ipc_handle, L.gdn_ipc_open, L.gdn_ipc_close, L.gdn_gather_push,
+                   L.gdn_gather_wait):
+            fn.restype = ctypes.c_int
         if path is None:
             _lib = L
         return L

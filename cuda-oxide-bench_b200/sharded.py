@@ -11,6 +11,7 @@ layer BASELINE config 4 adds.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable
 
@@ -109,3 +110,102 @@ class ShardedGDNDecoder:
             dist.all_gather(list(buf.unbind(0)), o_local, group=self.group)
         # rank-major -> head-major: [N, B, Hv/N, d_v] -> [B, N*Hv/N, d_v]
         return buf.permute(1, 0, 2, 3).reshape(self.B, self.Hv, o_local.shape[-1])
+
+
+class PeerGather:
+    """All-gather of equal per-rank slices with the copy engines over NVLink.
+
+    Every rank holds two slots of a rank-major buffer ``[2][N][slice]`` plus
+    ``ready[N]`` and ``free[N]`` step counters, all exported through CUDA IPC.
+    ``push(src, step)`` (on a side stream) waits until every rank has freed the
+    slot of ``step`` (used by ``step - 2``), copies ``src`` into slot
+    ``step % 2`` at row ``rank`` of every rank's buffer (DMA, no SMs), then
+    sets ``ready[rank] = step`` on every rank.  ``wait(step)`` makes a stream
+    wait until all ranks' slices of ``step`` have landed; ``release(step)``
+    tells every producer that this rank is done reading that slot.  Steps
+    start at 1.  All waits are GPU stream waits: no host synchronisation.
+    """
+
+    def __init__(self, slice_numel: int, dtype, device, group=None):
+        from . import _lib
+        self._lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        self.slice_numel = slice_numel
+        # one allocation (one IPC handle per rank): the two buffer slots, then
+        # the ready[N] | free[N] counters at a 256-byte boundary
+        esz = torch.empty((), dtype=dtype).element_size()
+        buf_bytes = 2 * self.world * slice_numel * esz
+        flag_off = (buf_bytes + 255) // 256 * 256
+        self.raw = torch.zeros(flag_off + 8 * self.world, dtype=torch.uint8, device=self.device)
+        self.buf = self.raw[:buf_bytes].view(dtype).view(2, self.world, slice_numel)
+        self.flags = self.raw[flag_off:].view(torch.int32)
+        h = self._handle(self.raw)
+        allh = [None] * self.world
+        dist.all_gather_object(allh, h, group=group)
+        self._opened = []
+        bases = []
+        for p, hp in enumerate(allh):
+            bases.append(self.raw.data_ptr() if p == self.rank else self._open(hp))
+        bufs = bases
+        flags = [bp + flag_off for bp in bases]
+        n = self.world
+        slice_bytes = slice_numel * esz
+        VP = ctypes.c_void_p * n
+        # destinations of this rank's slice in each slot, and the flag words it writes
+        self._dst = [VP(*[bufs[p] + (slot * n + self.rank) * slice_bytes for p in range(n)])
+                     for slot in range(2)]
+        self._ready = VP(*[flags[p] + 4 * self.rank for p in range(n)])
+        self._free = VP(*[flags[p] + 4 * (n + self.rank) for p in range(n)])
+        self._slice_bytes = slice_bytes
+        dist.barrier(group=group)
+
+    def _handle(self, t):
+        """(IPC handle of t's allocation, byte offset of t inside it)."""
+        from ._lib import IPC_HANDLE_BYTES, check
+        h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        off = ctypes.c_uint64()
+        check(self._lib.gdn_ipc_handle(t.data_ptr(), h, ctypes.byref(off)), "gdn_ipc_handle")
+        return h.raw, off.value
+
+    def _open(self, handle_and_offset) -> int:
+        from ._lib import check
+        handle, offset = handle_and_offset
+        ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+        check(self._lib.gdn_ipc_open(handle, offset, ctypes.byref(ptr), ctypes.byref(base)),
+              "gdn_ipc_open")
+        self._opened.append(base.value)
+        return ptr.value
+
+    @staticmethod
+    def _s(stream):
+        return (stream or torch.cuda.current_stream()).cuda_stream
+
+    def push(self, src: torch.Tensor, step: int, stream=None) -> None:
+        from ._lib import check
+        s = self._s(stream)
+        if step > 2:  # every consumer is done with the slot this step overwrites
+            check(self._lib.gdn_gather_wait(self.flags.data_ptr() + 4 * self.world, self.world,
+                                            step - 2, s), "gdn_gather_wait")
+        check(self._lib.gdn_gather_push(src.data_ptr(), self._slice_bytes, self._dst[step % 2],
+                                        self._ready, self.world, step, s), "gdn_gather_push")
+
+    def wait(self, step: int, stream=None) -> torch.Tensor:
+        """Stream-waits for every slice of ``step``; returns the slot [N, slice]."""
+        from ._lib import check
+        check(self._lib.gdn_gather_wait(self.flags.data_ptr(), self.world, step, self._s(stream)),
+              "gdn_gather_wait")
+        return self.buf[step % 2]
+
+    def release(self, step: int, stream=None) -> None:
+        from ._lib import check
+        # zero-byte copies, then the free-flag writes on every producer
+        check(self._lib.gdn_gather_push(self.flags.data_ptr(), 0, self._free, self._free,
+                                        self.world, step, self._s(stream)), "gdn_gather_push")
+
+    def close(self) -> None:
+        for p in self._opened:
+            self._lib.gdn_ipc_close(p)
+        self._opened = []

@@ -193,6 +193,35 @@ size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args);
  */
 int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Multi-GPU: all-gather of per-rank decode outputs with the copy engines.
+ * The reference is single-GPU (METHODOLOGY.md:80); these entry points have no
+ * counterpart there.  They serve value-head-sharded decode with one process
+ * per GPU on one NVLink node.
+ * ---------------------------------------------------------------------- */
+#define GDN_IPC_HANDLE_BYTES 64
+
+/* Exports a CUDA IPC handle (GDN_IPC_HANDLE_BYTES bytes) for the allocation
+ * containing dev_ptr, and dev_ptr's byte offset inside that allocation. */
+int gdn_ipc_handle(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+
+/* Maps a peer process's allocation into this process (current device; peer
+ * access is enabled on demand): *dev_ptr_out = mapped base + offset.  Close
+ * with gdn_ipc_close(*base_out). */
+int gdn_ipc_open(const void* handle, uint64_t offset, void** dev_ptr_out, void** base_out);
+int gdn_ipc_close(void* base);
+
+/* On `stream`: copy `bytes` from `src` into each peer_dst[i] (cudaMemcpyAsync,
+ * a DMA over NVLink, no SMs), then write `value` into each *peer_flag[i].  The
+ * flag writes are ordered after all copies on the stream. */
+int gdn_gather_push(const void* src, size_t bytes, void* const* peer_dst,
+                    uint32_t* const* peer_flag, int32_t n_peers, uint32_t value,
+                    gdn_stream_t stream);
+
+/* Makes `stream` wait (on the GPU front end) until flags[i] >= value for all
+ * i < n. */
+int gdn_gather_wait(const uint32_t* flags, int32_t n, uint32_t value, gdn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,3 +74,51 @@ def test_sharded_decode_two_gpus_matches_single(pkg, inputs):
         assert p.exitcode == 0
     np.testing.assert_allclose(o, ref_o, rtol=1e-2, atol=1e-2)
     assert np.abs(s - ref_s).max() < 1e-5
+
+
+def _gather_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        sh = graft.submodule("sharded")
+        dev = torch.device("cuda", rank)
+        n = 4096 + 8
+        pg = sh.PeerGather(n, torch.bfloat16, dev)
+        side = torch.cuda.Stream(dev)
+        ok = True
+        for step in range(1, 7):
+            src = torch.full((n,), float(100 * step + rank), dtype=torch.bfloat16, device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            pg.push(src, step, side)
+            got = pg.wait(step, side)
+            with torch.cuda.stream(side):
+                snap = got.clone()
+            pg.release(step, side)
+            side.synchronize()
+            want = torch.tensor([100.0 * step + r for r in range(world)]).view(world, 1).expand(world, n)
+            want = want.to(torch.bfloat16).float()  # same rounding as the pushed data
+            ok = ok and torch.equal(snap.float().cpu(), want)
+        dist.barrier()
+        pg.close()
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_copy_engine_gather_two_gpus():
+    """The copy-engine all-gather delivers every rank's slice, step after step,
+    through both buffer slots."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res == {0: True, 1: True}
