@@ -225,7 +225,8 @@ def run_gpu(args, world, rank, local):
     # decode of step i + 1; step i + 2 waits for it before reusing the buffer
     outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     out = outs[0]
-    ce = world > 1 and args.gather == "ce"
+    gmode = args.gather if args.gather != "auto" else ("ce" if world == 2 else "nccl")
+    ce = world > 1 and gmode == "ce"
     res = args.sm_reserve if args.sm_reserve >= 0 else min(48, 8 * world if world > 2 else 16)
     res = res if (world > 1 and not ce) else 0
     steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
@@ -244,6 +245,7 @@ def run_gpu(args, world, rank, local):
         # its output buffer
         pg = sharded.PeerGather(B * hv * D, torch.bfloat16, dev)
         side = torch.cuda.Stream(dev)
+        peer_streams = [torch.cuda.Stream(dev) for _ in range(world)]  # one copy engine each
         ev_dec = [torch.cuda.Event() for _ in range(2)]
         ev_out_free = [None, None]
         gstep = [0]
@@ -253,8 +255,11 @@ def run_gpu(args, world, rank, local):
             gstep[0] += 1
             ms_ = torch.cuda.current_stream(dev)
             ev_dec[i % 2].record(ms_)
-            side.wait_event(ev_dec[i % 2])
-            pg.push(outs[i % 2], gstep[0], side)
+            for ps in peer_streams:
+                ps.wait_event(ev_dec[i % 2])
+            pg.push(outs[i % 2], gstep[0], peer_streams=peer_streams)
+            for ps in peer_streams:
+                side.wait_stream(ps)
             ev = torch.cuda.Event()
             ev.record(side)
             ev_out_free[i % 2] = ev
@@ -577,8 +582,9 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the decode leaves to the overlapped all-gather (N>1); default "
                          "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
-    ap.add_argument("--gather", default="ce", choices=("ce", "nccl"),
-                    help="N>1 output all-gather: copy engines over NVLink (ce) or NCCL")
+    ap.add_argument("--gather", default="auto", choices=("auto", "ce", "nccl"),
+                    help="N>1 output all-gather: copy engines over NVLink (ce) or NCCL; auto "
+                         "picks the measured faster one (ce at N=2, NCCL + SM reservation at N>=4)")
     ap.add_argument("--no-graph", action="store_true",
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",

@@ -183,14 +183,29 @@ class PeerGather:
     def _s(stream):
         return (stream or torch.cuda.current_stream()).cuda_stream
 
-    def push(self, src: torch.Tensor, step: int, stream=None) -> None:
+    def push(self, src: torch.Tensor, step: int, stream=None, peer_streams=None) -> None:
+        """Sends ``src`` to every rank.  With ``peer_streams`` (one stream per
+        rank) the copies to different ranks run on separate copy engines in
+        parallel; otherwise they queue on ``stream``."""
         from ._lib import check
-        s = self._s(stream)
-        if step > 2:  # every consumer is done with the slot this step overwrites
-            check(self._lib.gdn_gather_wait(self.flags.data_ptr() + 4 * self.world, self.world,
-                                            step - 2, s), "gdn_gather_wait")
-        check(self._lib.gdn_gather_push(src.data_ptr(), self._slice_bytes, self._dst[step % 2],
-                                        self._ready, self.world, step, s), "gdn_gather_push")
+        n = self.world
+        if peer_streams is None:
+            s = self._s(stream)
+            if step > 2:  # every consumer is done with the slot this step overwrites
+                check(self._lib.gdn_gather_wait(self.flags.data_ptr() + 4 * n, n, step - 2, s),
+                      "gdn_gather_wait")
+            check(self._lib.gdn_gather_push(src.data_ptr(), self._slice_bytes, self._dst[step % 2],
+                                            self._ready, n, step, s), "gdn_gather_push")
+            return
+        VP1 = ctypes.c_void_p * 1
+        for p in range(n):
+            s = peer_streams[p].cuda_stream
+            if step > 2:  # rank p is done with the slot this step overwrites
+                check(self._lib.gdn_gather_wait(self.flags.data_ptr() + 4 * (n + p), 1, step - 2, s),
+                      "gdn_gather_wait")
+            check(self._lib.gdn_gather_push(src.data_ptr(), self._slice_bytes,
+                                            VP1(self._dst[step % 2][p]), VP1(self._ready[p]), 1,
+                                            step, s), "gdn_gather_push")
 
     def wait(self, step: int, stream=None) -> torch.Tensor:
         """Stream-waits for every slice of ``step``; returns the slot [N, slice]."""

@@ -86,11 +86,19 @@ def _gather_worker(rank, world, port, q):
         n = 4096 + 8
         pg = sh.PeerGather(n, torch.bfloat16, dev)
         side = torch.cuda.Stream(dev)
+        peers = [torch.cuda.Stream(dev) for _ in range(world)]
         ok = True
         for step in range(1, 7):
             src = torch.full((n,), float(100 * step + rank), dtype=torch.bfloat16, device=dev)
             side.wait_stream(torch.cuda.current_stream(dev))
-            pg.push(src, step, side)
+            if step % 2:
+                pg.push(src, step, side)
+            else:  # one stream (copy engine) per destination rank
+                for ps in peers:
+                    ps.wait_stream(side)
+                pg.push(src, step, peer_streams=peers)
+                for ps in peers:
+                    side.wait_stream(ps)
             got = pg.wait(step, side)
             with torch.cuda.stream(side):
                 snap = got.clone()
