@@ -601,17 +601,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_wait_ld();
 #pragma unroll
         for (int cb = 0; cb < 2; ++cb) {
-          float hi[16], lo[16];
+          // each pair is converted once; the packed hi word is reused for the
+          // tile and unpacked for the lo residual
+          uint32_t wp[8], wh[8], wl[8];
+          const float4* dec4 = reinterpret_cast<const float4*>(sDecay + half * 32 + cb * 16);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = half * 32 + cb * 16 + jj;
-            const float vd = u[cb * 16 + jj] * sDecay[j];
-            hi[jj] = tc::unpack_lo<BF16>(tc::pack2<BF16>(vd, 0.f));
-            lo[jj] = vd - hi[jj];
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 d = dec4[q4];
+            const float dd[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+              const int e = q4 * 2 + e2;
+              const float u0 = u[cb * 16 + 2 * e], u1 = u[cb * 16 + 2 * e + 1];
+              const float v0 = u0 * dd[2 * e2], v1 = u1 * dd[2 * e2 + 1];
+              wp[e] = tc::pack2<BF16>(u0, u1);
+              wh[e] = tc::pack2<BF16>(v0, v1);
+              wl[e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(wh[e]), v1 - tc::unpack_hi<BF16>(wh[e]));
+            }
           }
-          store_row16<BF16>(sb + kVP, dv, half * 4 + cb * 2, u + cb * 16);
-          store_row16<BF16>(sb + kVH, dv, half * 4 + cb * 2, hi);
-          store_row16<BF16>(sb + kVL, dv, half * 4 + cb * 2, lo);
+          const int ch = half * 4 + cb * 2;
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            tc::sts128(sb + kVP + tc::sw128_offset(dv, ch + k2), wp[4 * k2], wp[4 * k2 + 1],
+                       wp[4 * k2 + 2], wp[4 * k2 + 3]);
+            tc::sts128(sb + kVH + tc::sw128_offset(dv, ch + k2), wh[4 * k2], wh[4 * k2 + 1],
+                       wh[4 * k2 + 2], wh[4 * k2 + 3]);
+            tc::sts128(sb + kVL + tc::sw128_offset(dv, ch + k2), wl[4 * k2], wl[4 * k2 + 1],
+                       wl[4 * k2 + 2], wl[4 * k2 + 3]);
+          }
         }
       }
       tc::fence_proxy_async();
