@@ -16,6 +16,7 @@ LIB_PATH = _PKG_DIR / "libgdn_b200.so"
 # enums mirrored from include/gdn_b200.h
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 GATE_LOG, GATE_LINEAR = 0, 1
+DECODE_L2NORM_QK, DECODE_GATE_RAW = 1, 2
 OK = 0
 ERR_DEVICE_WAIT = 8
 
@@ -71,6 +72,10 @@ class DecodeArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("status", ctypes.c_void_p),
         ("sm_reserve", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("l2_eps", ctypes.c_float),
+        ("A_log", ctypes.c_void_p),
+        ("dt_bias", ctypes.c_void_p),
     ]
 
 

@@ -63,7 +63,8 @@ def _stream_ptr(dev: torch.device) -> int:
 
 
 def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
-                 sm_reserve: int = 0) -> _lib.DecodeArgs:
+                 sm_reserve: int = 0, l2norm_qk: bool = False, l2_eps: float = 1e-6,
+                 A_log=None, dt_bias=None) -> _lib.DecodeArgs:
     if q.dim() != 3 or k.shape != q.shape or v.dim() != 3:
         raise GDNError("q, k must be [B, Hqk, d_k] and v [B, Hv, d_v]", 2)
     B, Hqk, dk = q.shape
@@ -110,6 +111,19 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
     a.scale = float(scale)
     a.status = status_word(q.device).data_ptr()
     a.sm_reserve = int(sm_reserve)
+    a.flags = _lib.DECODE_L2NORM_QK if l2norm_qk else 0
+    a.l2_eps = float(l2_eps)
+    if (A_log is None) != (dt_bias is None):
+        raise GDNError("A_log and dt_bias go together (raw-gate mode)", 1)
+    if A_log is not None:
+        if kda:
+            raise GDNError("the raw-gate formula is the scalar GDN gate; not for KDA", 4)
+        for name, t in (("A_log", A_log), ("dt_bias", dt_bias)):
+            if t.dtype != torch.float32 or tuple(t.shape) != (Hv,) or not t.is_contiguous() \
+                    or t.device != q.device:
+                raise GDNError(f"{name} must be a contiguous fp32 [Hv] tensor on {q.device}", 2)
+        a.flags |= _lib.DECODE_GATE_RAW
+        a.A_log, a.dt_bias = A_log.data_ptr(), dt_bias.data_ptr()
     return a
 
 
@@ -120,14 +134,15 @@ class DecodeStep:
     must stay alive and in place while the object is used."""
 
     def __init__(self, q, k, v, g, beta, state, *, out=None, state_out=None, scale=1.0,
-                 gate="log", kda=False, sm_reserve=0):
+                 gate="log", kda=False, sm_reserve=0, l2norm_qk=False, l2_eps=1e-6,
+                 A_log=None, dt_bias=None):
         dev = _require_cuda(q, k, v, g, beta, state)
         self.out = out if out is not None else torch.empty(
             (v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
         state_out = state if state_out is None else state_out
-        self._keep = (q, k, v, g, beta, state, state_out, self.out)
+        self._keep = (q, k, v, g, beta, state, state_out, self.out, A_log, dt_bias)
         self._args = _decode_args(q, k, v, g, beta, state, state_out, self.out, scale, gate, kda,
-                                  sm_reserve)
+                                  sm_reserve, l2norm_qk, l2_eps, A_log, dt_bias)
         self._argp = ctypes.byref(self._args)
         L = _lib.load()
         self._fn = L.kda_decode_launch if kda else L.gdn_decode_launch
@@ -142,7 +157,9 @@ class DecodeStep:
 
 
 def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: str = "log",
-               state_out=None, check: bool = False, sm_reserve: int = 0) -> torch.Tensor:
+               state_out=None, check: bool = False, sm_reserve: int = 0,
+               l2norm_qk: bool = False, l2_eps: float = 1e-6, A_log=None,
+               dt_bias=None) -> torch.Tensor:
     """One GDN decode step; ``state`` is updated in place (or written to
     ``state_out``).  Returns o [B, Hv, d_v] in q's dtype.
 
@@ -151,12 +168,18 @@ def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: s
     ``check=True`` synchronises and raises on a device-side failure.
     ``sm_reserve`` leaves that many SMs free for a concurrent kernel (the
     persistent decode otherwise occupies every SM).
+
+    Fused layer preprocessing: ``l2norm_qk=True`` L2-normalises q and k per
+    head inside the kernel (x / sqrt(sum x^2 + l2_eps)); with ``A_log`` and
+    ``dt_bias`` ([Hv] fp32) ``g`` is the raw gate projection ``a`` and the log
+    gate is -exp(A_log) * softplus(a + dt_bias).
     """
     dev = _require_cuda(q, k, v, g, beta, state)
     if out is None:
         out = torch.empty((v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
     so = state if state_out is None else state_out
-    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, False, sm_reserve)
+    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, False, sm_reserve,
+                     l2norm_qk, l2_eps, A_log, dt_bias)
     _lib.check(_lib.load().gdn_decode_launch(ctypes.byref(a), _stream_ptr(dev)), "gdn_decode")
     if check:
         check_device_status(dev)
@@ -164,14 +187,15 @@ def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: s
 
 
 def kda_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: str = "log",
-               state_out=None, check: bool = False) -> torch.Tensor:
+               state_out=None, check: bool = False, l2norm_qk: bool = False,
+               l2_eps: float = 1e-6) -> torch.Tensor:
     """One KDA decode step (per-channel gate g [B, Hv, d_k]); otherwise as
-    :func:`gdn_decode`."""
+    :func:`gdn_decode` (``l2norm_qk`` included; no raw-gate mode)."""
     dev = _require_cuda(q, k, v, g, beta, state)
     if out is None:
         out = torch.empty((v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
     so = state if state_out is None else state_out
-    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, True)
+    a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, True, 0, l2norm_qk, l2_eps)
     _lib.check(_lib.load().kda_decode_launch(ctypes.byref(a), _stream_ptr(dev)), "kda_decode")
     if check:
         check_device_status(dev)

@@ -78,7 +78,10 @@ struct DecodeTraits {
   static_assert(DK % kRowGroups == 0, "DK must be a multiple of the row groups");
 };
 
-template <int DK, int BV, typename IO, bool KDA>
+// PRE: the fused layer-preprocessing variant (in-kernel q/k L2 norm, gate from
+// the raw projection), a separate instantiation so the plain kernel carries
+// none of its code.
+template <int DK, int BV, typename IO, bool KDA, bool PRE>
 __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
                                   DecodeTraits<DK, BV, KDA>::kCtasPerSm)
     decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap state_map) {
@@ -192,7 +195,14 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
     float alpha = 1.f;
     if (!KDA) {
       const float g = load_any(a.g, b * a.g_sb + static_cast<int64_t>(h) * a.g_sh, a.g_dtype);
-      alpha = (a.gate_kind == GDN_GATE_LOG) ? __expf(g) : g;
+      if (PRE && (a.flags & GDN_DECODE_GATE_RAW)) {
+        // log gate from the raw projection: -exp(A_log) * softplus(a + dt_bias)
+        const float x = g + __ldg(a.dt_bias + h);
+        const float sp = x > 20.f ? x : log1pf(expf(x));
+        alpha = expf(-expf(__ldg(a.A_log + h)) * sp);
+      } else {
+        alpha = (a.gate_kind == GDN_GATE_LOG) ? __expf(g) : g;
+      }
     }
 
     // A timed-out thread still runs to the reduction barrier below, where the
@@ -236,6 +246,22 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
     vv.y = to_f32(s_v[cg * 4 + 1]);
     vv.z = to_f32(s_v[cg * 4 + 2]);
     vv.w = to_f32(s_v[cg * 4 + 3]);
+    // |q|^2 and |k|^2 for the in-kernel L2 normalisation: every warp sums the
+    // staged rows itself (no extra state in the row loop, nothing when off)
+    float qq = 0.f, kk = 0.f;
+    if (PRE && (a.flags & GDN_DECODE_L2NORM_QK)) {
+#pragma unroll
+      for (int e = lane; e < DK; e += 32) {
+        const float qe = to_f32(s_q[e]), ke = to_f32(s_k[e]);
+        qq = fmaf(qe, qe, qq);
+        kk = fmaf(ke, ke, kk);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        qq += __shfl_xor_sync(0xffffffffu, qq, off);
+        kk += __shfl_xor_sync(0xffffffffu, kk, off);
+      }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);  // slot may be refilled now
 
@@ -276,6 +302,17 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
       qs.x += pq.x; qs.y += pq.y; qs.z += pq.z; qs.w += pq.w;
       qk += rq[w];
     }
+    // In-kernel L2 normalisation of q and k folds into the reduced scalars:
+    // every use of k (u, q.k, the update beta k r^T) and of q (q.S, q.k) is
+    // linear in it.
+    float rk = 1.f, rqn = 1.f;
+    if (PRE && (a.flags & GDN_DECODE_L2NORM_QK)) {
+      rk = rsqrtf(kk + a.l2_eps);
+      rqn = rsqrtf(qq + a.l2_eps);
+      u.x *= rk; u.y *= rk; u.z *= rk; u.w *= rk;
+      qs.x *= rqn; qs.y *= rqn; qs.z *= rqn; qs.w *= rqn;
+      qk *= rqn * rk;
+    }
     float4 r;
     r.x = vv.x - u.x; r.y = vv.y - u.y; r.z = vv.z - u.z; r.w = vv.w - u.w;
 
@@ -295,7 +332,7 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
 #pragma unroll
     for (int i = 0; i < Tr::kRows; ++i) {
       const int row = rg + i * Tr::kRowGroups;
-      const float bk = beta * kr[i];
+      const float bk = PRE ? beta * rk * kr[i] : beta * kr[i];
       float4 x = s[i];
       x.x = fmaf(bk, r.x, x.x); x.y = fmaf(bk, r.y, x.y);
       x.z = fmaf(bk, r.z, x.z); x.w = fmaf(bk, r.w, x.w);
@@ -306,7 +343,7 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
 
 // ------------------------------------------------------------------ launcher
 
-template <int DK, int BV, typename IO, bool KDA>
+template <int DK, int BV, typename IO, bool KDA, bool PRE>
 static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   using Tr = DecodeTraits<DK, BV, KDA>;
   static std::atomic<uint64_t> attr_done{0};
@@ -320,7 +357,7 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   if (stages > Tr::kMaxStages) stages = Tr::kMaxStages;
   if (stages < 2) return GDN_ERR_SHAPE;
   const int smem = Tr::kHeaderBytes + 128 + stages * Tr::kStageBytes;
-  auto kern = decode_kernel<DK, BV, IO, KDA>;
+  auto kern = decode_kernel<DK, BV, IO, KDA, PRE>;
   rc = ensure_smem_attr(kern, smem, attr_done);
   if (rc) return rc;
 
@@ -356,6 +393,12 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
   if (a->io_dtype != GDN_DT_BF16 && a->io_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
   if (!dtype_valid(a->g_dtype) || !dtype_valid(a->beta_dtype)) return GDN_ERR_DTYPE;
   if (a->gate_kind != GDN_GATE_LOG && a->gate_kind != GDN_GATE_LINEAR) return GDN_ERR_DTYPE;
+  if (a->flags & ~(GDN_DECODE_L2NORM_QK | GDN_DECODE_GATE_RAW)) return GDN_ERR_DTYPE;
+  if (a->flags & GDN_DECODE_GATE_RAW) {
+    if (kda) return GDN_ERR_DTYPE;  // the raw-gate formula is the scalar GDN gate
+    if (!a->A_log || !a->dt_bias) return GDN_ERR_NULL;
+  }
+  if ((a->flags & GDN_DECODE_L2NORM_QK) && !(a->l2_eps >= 0.f)) return GDN_ERR_SHAPE;
   // bulk-copied rows: 16-byte aligned bases and strides
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) ||
       !aligned16(a->state_in) || !aligned16(a->state_out))
@@ -398,19 +441,24 @@ static int pick_bv(const gdn_decode_args_t& a, int sm_count) {
   return last;
 }
 
-template <typename IO, bool KDA>
+template <typename IO, bool KDA, bool PRE>
 static int dispatch_dk(const gdn_decode_args_t& a, cudaStream_t stream, int bv) {
   switch (a.dk) {
-    case 64: return launch_decode_impl<64, 64, IO, KDA>(a, stream);
+    case 64: return launch_decode_impl<64, 64, IO, KDA, PRE>(a, stream);
     case 128:
-      if (bv == 128) return launch_decode_impl<128, 128, IO, KDA>(a, stream);
-      if (bv == 64) return launch_decode_impl<128, 64, IO, KDA>(a, stream);
-      return launch_decode_impl<128, 32, IO, KDA>(a, stream);
+      if (bv == 128) return launch_decode_impl<128, 128, IO, KDA, PRE>(a, stream);
+      if (bv == 64) return launch_decode_impl<128, 64, IO, KDA, PRE>(a, stream);
+      return launch_decode_impl<128, 32, IO, KDA, PRE>(a, stream);
     case 256:
-      return bv == 64 ? launch_decode_impl<256, 64, IO, KDA>(a, stream)
-                      : launch_decode_impl<256, 32, IO, KDA>(a, stream);
+      return bv == 64 ? launch_decode_impl<256, 64, IO, KDA, PRE>(a, stream)
+                      : launch_decode_impl<256, 32, IO, KDA, PRE>(a, stream);
   }
   return GDN_ERR_SHAPE;
+}
+
+template <typename IO, bool KDA>
+static int dispatch_pre(const gdn_decode_args_t& a, cudaStream_t stream, int bv) {
+  return a.flags ? dispatch_dk<IO, KDA, true>(a, stream, bv) : dispatch_dk<IO, KDA, false>(a, stream, bv);
 }
 
 static int decode_entry(const gdn_decode_args_t* a, cudaStream_t stream, bool kda) {
@@ -421,9 +469,9 @@ static int decode_entry(const gdn_decode_args_t* a, cudaStream_t stream, bool kd
   if (rc) return rc;
   const int bv = pick_bv(*a, di.sm_count);
   if (a->io_dtype == GDN_DT_BF16)
-    return kda ? dispatch_dk<__nv_bfloat16, true>(*a, stream, bv)
-               : dispatch_dk<__nv_bfloat16, false>(*a, stream, bv);
-  return kda ? dispatch_dk<__half, true>(*a, stream, bv) : dispatch_dk<__half, false>(*a, stream, bv);
+    return kda ? dispatch_pre<__nv_bfloat16, true>(*a, stream, bv)
+               : dispatch_pre<__nv_bfloat16, false>(*a, stream, bv);
+  return kda ? dispatch_pre<__half, true>(*a, stream, bv) : dispatch_pre<__half, false>(*a, stream, bv);
 }
 
 }  // namespace gdn

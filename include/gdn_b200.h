@@ -68,6 +68,13 @@ enum {
   GDN_ERR_DEVICE_WAIT = 8, /* a device-side wait timed out (from the status)    */
 };
 
+/* decode option flags (gdn_decode_args_t.flags) */
+enum {
+  GDN_DECODE_L2NORM_QK = 1u << 0, /* q, k <- x / sqrt(sum x^2 + l2_eps) in-kernel    */
+  GDN_DECODE_GATE_RAW = 1u << 1,  /* g is the raw gate projection a:                */
+                                  /*   log gate = -exp(A_log[h]) softplus(a + dt_bias[h]) */
+};
+
 /* device-side status bits (OR-ed into *status) */
 enum {
   GDN_DEVERR_FULL_TIMEOUT = 1u << 0,  /* consumer waited too long for a slab      */
@@ -104,6 +111,10 @@ typedef struct {
   uint32_t* status;     /* optional device word for GDN_DEVERR_* bits        */
   int32_t sm_reserve;   /* SMs left free for concurrent kernels (e.g. an     */
                         /* NCCL collective overlapping the step); 0 = none   */
+  int32_t flags;        /* GDN_DECODE_* options (0 = none)                   */
+  float l2_eps;         /* epsilon of GDN_DECODE_L2NORM_QK                   */
+  const float* A_log;   /* [Hv] fp32, with GDN_DECODE_GATE_RAW (GDN only)    */
+  const float* dt_bias; /* [Hv] fp32, with GDN_DECODE_GATE_RAW               */
 } gdn_decode_args_t;
 
 /*

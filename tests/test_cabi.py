@@ -86,12 +86,15 @@ def _valid_args(pkg, **over):
     ({"gate_kind": 5}, 4),
     ({"q": 0x7F0000000008}, 3),  # 8-byte aligned only
     ({"v_sh": 100}, 3),          # 200-byte head stride
+    ({"flags": 8}, 4),           # unknown option bit
+    ({"flags": 2}, 1),           # raw gate without A_log / dt_bias
+    ({"flags": 1, "l2_eps": -1.0}, 2),
 ])
 def test_decode_validation_rejects(pkg, over, code):
     L = pkg._lib.load()
     a = _valid_args(pkg, **over)
     assert L.gdn_decode_launch(ctypes.byref(a), None) == code
-    assert L.kda_decode_launch(ctypes.byref(a), None) in (code, 3)
+    assert L.kda_decode_launch(ctypes.byref(a), None) in (code, 3, 4)
 
 
 def test_overlapping_out_of_place_state_rejected(pkg):

@@ -217,3 +217,43 @@ def test_bad_shapes_raise(pkg):
         pkg.gdn_decode(q, q, v, g, g, S)  # Hv=3 not a multiple of Hqk=2
     with pytest.raises(pkg.GDNError):
         pkg.gdn_decode(q.float(), q.float(), v.float(), g, g, S)  # fp32 I/O
+
+
+def test_fused_layer_preprocessing(pkg, inputs, orc):
+    """Raw projections in, fused preprocessing in the kernel: q/k L2-normalised
+    per head and the log gate computed from the raw gate projection a as
+    -exp(A_log) * softplus(a + dt_bias), against the oracle fed with the
+    preprocessed values."""
+    import torch.nn.functional as F
+    steps, B, Hqk, Hv, d = 8, 4, 2, 4, 128
+    gen = torch.Generator().manual_seed(31)
+    q = (torch.randn((steps, B, Hqk, d), generator=gen) * 3).to(torch.bfloat16)
+    k = (torch.randn((steps, B, Hqk, d), generator=gen) * 3).to(torch.bfloat16)
+    v = torch.randn((steps, B, Hv, d), generator=gen).to(torch.bfloat16)
+    a = torch.randn((steps, B, Hv), generator=gen)
+    beta = torch.sigmoid(torch.randn((steps, B, Hv), generator=gen))
+    A_log = torch.log(1 + 15 * torch.rand(Hv, generator=gen))
+    dt_bias = -4 + 3 * torch.rand(Hv, generator=gen)
+    S0 = torch.randn((B, Hv, d, d), generator=gen) * 0.02
+    eps = 1e-6
+    nrm = lambda x: x.float() / torch.sqrt((x.float() ** 2).sum(-1, keepdim=True) + eps)
+    g = -torch.exp(A_log) * F.softplus(a + dt_bias)
+    o_ref, s_ref = orc.gdn_decode_steps(nrm(q), nrm(k), v, g, beta, S0)
+    st = S0.to(DEV)
+    Ad, dd = A_log.to(DEV), dt_bias.to(DEV)
+    for t in range(steps):
+        o = pkg.gdn_decode(q[t].to(DEV), k[t].to(DEV), v[t].to(DEV), a[t].to(DEV),
+                           beta[t].to(DEV), st, l2norm_qk=True, l2_eps=eps, A_log=Ad, dt_bias=dd)
+        np.testing.assert_allclose(o.float().cpu().numpy(), o_ref[t], rtol=O_RTOL, atol=O_ATOL)
+    pkg.check_device_status()
+    assert np.abs(st.cpu().numpy() - s_ref).max() < S_ATOL
+    # KDA with in-kernel L2 normalisation
+    x = inputs.make_decode_inputs(4, 2, 2, 2, 128, kda=True, seed=7)
+    qr, kr = (x.q.float() * 5).to(torch.bfloat16), (x.k.float() * 0.5).to(torch.bfloat16)
+    ko, ks = orc.kda_decode_steps(nrm(qr), nrm(kr), x.v, x.g, x.beta, x.state)
+    st = x.state.to(DEV)
+    for t in range(4):
+        o = pkg.kda_decode(qr[t].to(DEV), kr[t].to(DEV), x.v[t].to(DEV), x.g[t].to(DEV),
+                           x.beta[t].to(DEV), st, l2norm_qk=True, l2_eps=eps)
+        np.testing.assert_allclose(o.float().cpu().numpy(), ko[t], rtol=O_RTOL, atol=O_ATOL)
+    assert np.abs(st.cpu().numpy() - ks).max() < S_ATOL
