@@ -494,6 +494,17 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
         ex[f"config1_gdn_B{b}"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
                                    "us": round(ms * 1e3, 2)}
         del x, st, s1
+    # optional fp16 state (half the streamed state bytes) at the headline size
+    x = inputs.make_decode_inputs(1, B, HQK, HV, D, seed=1, device=dev)
+    st = x.state.to(torch.float16)
+    s1 = pkg.DecodeStep(x.q[0], x.k[0], x.v[0], x.g[0], x.beta[0], st)
+    ms = _time_graph(lambda: s1(), reps=50)
+    byts = inputs.gdn_decode_bytes(B, HQK, HV) - B * HV * D * D * 4  # state at 2 bytes
+    ex[f"fp16_state_gdn_B{B}"] = {"GBps": round(byts / (ms * 1e-3) / 1e9, 1),
+                                  "frac_of_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4),
+                                  "tokens_per_s": round(B / (ms * 1e-3), 1), "us": round(ms * 1e3, 2),
+                                  "note": "option, not the BASELINE fp32 state"}
+    del x, st, s1
     # config 2: KDA B=64, H=32, 64 steps per replay
     x = inputs.make_decode_inputs(64, 64, 32, 32, D, kda=True, seed=2, device=dev)
     st = x.state.clone()

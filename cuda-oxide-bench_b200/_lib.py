@@ -76,6 +76,7 @@ class DecodeArgs(ctypes.Structure):
         ("l2_eps", ctypes.c_float),
         ("A_log", ctypes.c_void_p),
         ("dt_bias", ctypes.c_void_p),
+        ("state_dtype", ctypes.c_int32),
     ]
 
 

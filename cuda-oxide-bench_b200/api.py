@@ -81,8 +81,9 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
     if tuple(beta.shape) != (B, Hv):
         raise GDNError(f"beta must be [B, Hv] = {(B, Hv)}, got {tuple(beta.shape)}", 2)
     for name, t in (("state", state), ("state_out", state_out)):
-        if t.dtype != torch.float32 or tuple(t.shape) != (B, Hv, dk, dv) or not t.is_contiguous():
-            raise GDNError(f"{name} must be a contiguous fp32 [B, Hv, d_k, d_v] = "
+        if t.dtype not in (torch.float32, torch.float16) or t.dtype != state.dtype \
+                or tuple(t.shape) != (B, Hv, dk, dv) or not t.is_contiguous():
+            raise GDNError(f"{name} must be a contiguous fp32 (or fp16) [B, Hv, d_k, d_v] = "
                            f"{(B, Hv, dk, dv)} tensor", 2)
     if tuple(o.shape) != (B, Hv, dv) or o.dtype != q.dtype:
         raise GDNError("out must be [B, Hv, d_v] with the dtype of q", 2)
@@ -111,6 +112,7 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
     a.scale = float(scale)
     a.status = status_word(q.device).data_ptr()
     a.sm_reserve = int(sm_reserve)
+    a.state_dtype = _lib.DT_F16 if state.dtype == torch.float16 else _lib.DT_F32
     a.flags = _lib.DECODE_L2NORM_QK if l2norm_qk else 0
     a.l2_eps = float(l2_eps)
     if (A_log is None) != (dt_bias is None):

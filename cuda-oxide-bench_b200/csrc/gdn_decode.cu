@@ -52,7 +52,9 @@ struct DecodeParams {
   int32_t g_row_bytes;
 };
 
-template <int DK, int BV, bool KDA>
+// SB: bytes per state element (4 = fp32, the default; 2 = the optional fp16
+// state, which halves the bytes a step streams).
+template <int DK, int BV, bool KDA, int SB = 4>
 struct DecodeTraits {
   static constexpr int kConsumerWarps = 8;
   static constexpr int kConsumers = kConsumerWarps * 32;
@@ -65,7 +67,7 @@ struct DecodeTraits {
   // slabs back to back and each slab's reduction latency is exposed: those
   // variants run two CTAs per SM (fewer registers, half the smem ring each).
   static constexpr int kCtasPerSm = BV == 32 ? 2 : 1;
-  static constexpr uint32_t kSlabBytes = DK * BV * 4;
+  static constexpr uint32_t kSlabBytes = DK * BV * SB;
   static constexpr uint32_t kQKBytes = DK * 2;
   static constexpr uint32_t kVBytes = BV * 2;
   static constexpr uint32_t kGBytes = KDA ? DK * 4 : 0;  // room for an fp32 gate row
@@ -81,11 +83,11 @@ struct DecodeTraits {
 // PRE: the fused layer-preprocessing variant (in-kernel q/k L2 norm, gate from
 // the raw projection), a separate instantiation so the plain kernel carries
 // none of its code.
-template <int DK, int BV, typename IO, bool KDA, bool PRE>
-__global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
-                                  DecodeTraits<DK, BV, KDA>::kCtasPerSm)
+template <int DK, int BV, typename IO, bool KDA, bool PRE, int SB>
+__global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
+                                  DecodeTraits<DK, BV, KDA, SB>::kCtasPerSm)
     decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap state_map) {
-  using Tr = DecodeTraits<DK, BV, KDA>;
+  using Tr = DecodeTraits<DK, BV, KDA, SB>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + Tr::kMaxStages;
@@ -131,7 +133,8 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
       const int h = static_cast<int>(bh - b * a.Hv);
       const int hq = h / p.group;
       unsigned char* st = ring + static_cast<size_t>(stage) * p.stage_bytes;
-      const float* src = a.state_in + (bh * DK) * a.dv + static_cast<int64_t>(vb) * BV;
+      const unsigned char* src = reinterpret_cast<const unsigned char*>(a.state_in) +
+                                 ((bh * DK) * a.dv + static_cast<int64_t>(vb) * BV) * SB;
       if (lane == 0) {
         uint32_t bytes = 2 * Tr::kQKBytes + Tr::kVBytes + Tr::kSlabBytes;
         if (KDA) bytes += p.g_row_bytes;
@@ -224,7 +227,15 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
 #pragma unroll
     for (int i = 0; i < Tr::kRows; ++i) {
       const int row = rg + i * Tr::kRowGroups;
-      float4 x = lds128(s_slab + row * BV + cg * 4);
+      float4 x;
+      if (SB == 4) {
+        x = lds128(s_slab + row * BV + cg * 4);
+      } else {  // fp16 state: 4 halves (8 bytes), widened to fp32
+        const uint2 w = *reinterpret_cast<const uint2*>(st + (row * BV + cg * 4) * 2);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+        x = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
       const float kv = to_f32(s_k[row]);
       const float qv = to_f32(s_q[row]);
       float ai = alpha;
@@ -328,7 +339,8 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
       *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(ov);
     }
 
-    float* dst = a.state_out + (bh * DK) * a.dv + static_cast<int64_t>(vb) * BV + cg * 4;
+    unsigned char* dst = reinterpret_cast<unsigned char*>(a.state_out) +
+                         ((bh * DK) * a.dv + static_cast<int64_t>(vb) * BV + cg * 4) * SB;
 #pragma unroll
     for (int i = 0; i < Tr::kRows; ++i) {
       const int row = rg + i * Tr::kRowGroups;
@@ -336,16 +348,25 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA>::kThreads,
       float4 x = s[i];
       x.x = fmaf(bk, r.x, x.x); x.y = fmaf(bk, r.y, x.y);
       x.z = fmaf(bk, r.z, x.z); x.w = fmaf(bk, r.w, x.w);
-      stg128(dst + static_cast<int64_t>(row) * a.dv, x);
+      unsigned char* drow = dst + static_cast<int64_t>(row) * a.dv * SB;
+      if (SB == 4) {
+        stg128(reinterpret_cast<float*>(drow), x);
+      } else {
+        const __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
+        asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(drow),
+                     "r"(*reinterpret_cast<const uint32_t*>(&lo)),
+                     "r"(*reinterpret_cast<const uint32_t*>(&hi))
+                     : "memory");
+      }
     }
   }
 }
 
 // ------------------------------------------------------------------ launcher
 
-template <int DK, int BV, typename IO, bool KDA, bool PRE>
+template <int DK, int BV, typename IO, bool KDA, bool PRE, int SB>
 static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
-  using Tr = DecodeTraits<DK, BV, KDA>;
+  using Tr = DecodeTraits<DK, BV, KDA, SB>;
   static std::atomic<uint64_t> attr_done{0};
   DeviceInfo di;
   int rc = device_info(&di);
@@ -357,7 +378,7 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   if (stages > Tr::kMaxStages) stages = Tr::kMaxStages;
   if (stages < 2) return GDN_ERR_SHAPE;
   const int smem = Tr::kHeaderBytes + 128 + stages * Tr::kStageBytes;
-  auto kern = decode_kernel<DK, BV, IO, KDA, PRE>;
+  auto kern = decode_kernel<DK, BV, IO, KDA, PRE, SB>;
   rc = ensure_smem_attr(kern, smem, attr_done);
   if (rc) return rc;
 
@@ -373,7 +394,11 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
   if (!p.contiguous) {
-    rc = fp32_tensor_map_2d(&map, a.state_in, static_cast<uint64_t>(a.B) * a.Hv * DK, a.dv, DK, BV);
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.dv), static_cast<uint64_t>(a.B) * a.Hv * DK};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.dv) * SB};
+    const uint32_t box[2] = {BV, DK};
+    rc = tensor_map(&map, SB == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                    2, a.state_in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
   int ctas = (di.sm_count - (a.sm_reserve > 0 ? a.sm_reserve : 0)) * Tr::kCtasPerSm;
@@ -394,6 +419,7 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
   if (!dtype_valid(a->g_dtype) || !dtype_valid(a->beta_dtype)) return GDN_ERR_DTYPE;
   if (a->gate_kind != GDN_GATE_LOG && a->gate_kind != GDN_GATE_LINEAR) return GDN_ERR_DTYPE;
   if (a->flags & ~(GDN_DECODE_L2NORM_QK | GDN_DECODE_GATE_RAW)) return GDN_ERR_DTYPE;
+  if (a->state_dtype != GDN_DT_F32 && a->state_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
   if (a->flags & GDN_DECODE_GATE_RAW) {
     if (kda) return GDN_ERR_DTYPE;  // the raw-gate formula is the scalar GDN gate
     if (!a->A_log || !a->dt_bias) return GDN_ERR_NULL;
@@ -413,9 +439,10 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
   }
   // in place, or fully disjoint
   if (a->state_in != a->state_out) {
-    const size_t n = static_cast<size_t>(a->B) * a->Hv * a->dk * a->dv;
-    const float* i0 = a->state_in;
-    const float* o0 = a->state_out;
+    const size_t n = static_cast<size_t>(a->B) * a->Hv * a->dk * a->dv *
+                     (a->state_dtype == GDN_DT_F16 ? 2 : 4);
+    const char* i0 = reinterpret_cast<const char*>(a->state_in);
+    const char* o0 = reinterpret_cast<const char*>(a->state_out);
     if (i0 < o0 + n && o0 < i0 + n) return GDN_ERR_SHAPE;
   }
   return GDN_OK;
@@ -443,15 +470,21 @@ static int pick_bv(const gdn_decode_args_t& a, int sm_count) {
 
 template <typename IO, bool KDA, bool PRE>
 static int dispatch_dk(const gdn_decode_args_t& a, cudaStream_t stream, int bv) {
+  if (a.state_dtype == GDN_DT_F16) {  // fp16 state: d = 128 only
+    if (a.dk != 128) return GDN_ERR_SHAPE;
+    if (bv == 128) return launch_decode_impl<128, 128, IO, KDA, PRE, 2>(a, stream);
+    if (bv == 64) return launch_decode_impl<128, 64, IO, KDA, PRE, 2>(a, stream);
+    return launch_decode_impl<128, 32, IO, KDA, PRE, 2>(a, stream);
+  }
   switch (a.dk) {
-    case 64: return launch_decode_impl<64, 64, IO, KDA, PRE>(a, stream);
+    case 64: return launch_decode_impl<64, 64, IO, KDA, PRE, 4>(a, stream);
     case 128:
-      if (bv == 128) return launch_decode_impl<128, 128, IO, KDA, PRE>(a, stream);
-      if (bv == 64) return launch_decode_impl<128, 64, IO, KDA, PRE>(a, stream);
-      return launch_decode_impl<128, 32, IO, KDA, PRE>(a, stream);
+      if (bv == 128) return launch_decode_impl<128, 128, IO, KDA, PRE, 4>(a, stream);
+      if (bv == 64) return launch_decode_impl<128, 64, IO, KDA, PRE, 4>(a, stream);
+      return launch_decode_impl<128, 32, IO, KDA, PRE, 4>(a, stream);
     case 256:
-      return bv == 64 ? launch_decode_impl<256, 64, IO, KDA, PRE>(a, stream)
-                      : launch_decode_impl<256, 32, IO, KDA, PRE>(a, stream);
+      return bv == 64 ? launch_decode_impl<256, 64, IO, KDA, PRE, 4>(a, stream)
+                      : launch_decode_impl<256, 32, IO, KDA, PRE, 4>(a, stream);
   }
   return GDN_ERR_SHAPE;
 }

@@ -97,7 +97,8 @@ typedef struct {
   const void* v;        /* [B, Hv,  d_v]   io_dtype                         */
   const void* g;        /* GDN: [B, Hv]; KDA: [B, Hv, d_k]   g_dtype        */
   const void* beta;     /* [B, Hv]         beta_dtype                       */
-  const float* state_in;/* [B, Hv, d_k, d_v] fp32 contiguous                */
+  const float* state_in;/* [B, Hv, d_k, d_v] contiguous, fp32 (or fp16, see */
+                        /* state_dtype; the pointer is then reinterpreted)  */
   float* state_out;     /* same layout; may equal state_in (in place)       */
   void* o;              /* [B, Hv, d_v]    io_dtype                         */
   int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh, o_sb, o_sh;
@@ -115,6 +116,9 @@ typedef struct {
   float l2_eps;         /* epsilon of GDN_DECODE_L2NORM_QK                   */
   const float* A_log;   /* [Hv] fp32, with GDN_DECODE_GATE_RAW (GDN only)    */
   const float* dt_bias; /* [Hv] fp32, with GDN_DECODE_GATE_RAW               */
+  int32_t state_dtype;  /* GDN_DT_F32 (default) or GDN_DT_F16 (d_k = 128):   */
+                        /* an fp16 state halves the bytes a step streams;    */
+                        /* arithmetic stays fp32                             */
 } gdn_decode_args_t;
 
 /*

@@ -257,3 +257,21 @@ def test_fused_layer_preprocessing(pkg, inputs, orc):
                            x.beta[t].to(DEV), st, l2norm_qk=True, l2_eps=eps)
         np.testing.assert_allclose(o.float().cpu().numpy(), ko[t], rtol=O_RTOL, atol=O_ATOL)
     assert np.abs(st.cpu().numpy() - ks).max() < S_ATOL
+
+
+@pytest.mark.parametrize("B,steps", [(8, 64), (64, 8), (10, 4)])
+def test_fp16_state_within_tolerance(pkg, inputs, orc, B, steps):
+    """Optional fp16 state (half the streamed bytes, fp32 arithmetic) against
+    the fp32 recurrence.  Outputs meet the BASELINE bf16 tolerance; the state
+    does NOT meet the BASELINE 1e-3 gate after 64 steps (1.25e-3 measured), so
+    this option is off by default and checked here against its own bound
+    (2e-3 max-abs).  Covers 32-, 64- and 128-column slabs."""
+    x = inputs.make_decode_inputs(steps, B, 16, 32, 128, seed=40 + B)
+    o_ref, s_ref = orc.gdn_decode_steps(x.q, x.k, x.v, x.g, x.beta, x.state)
+    st = x.state.to(DEV, torch.float16)
+    for t in range(steps):
+        o = pkg.gdn_decode(x.q[t].to(DEV), x.k[t].to(DEV), x.v[t].to(DEV), x.g[t].to(DEV),
+                           x.beta[t].to(DEV), st)
+        np.testing.assert_allclose(o.float().cpu().numpy(), o_ref[t], rtol=O_RTOL, atol=O_ATOL)
+    pkg.check_device_status()
+    assert np.abs(st.float().cpu().numpy() - s_ref).max() < 2e-3  # fp16-state bound, see docstring
