@@ -30,6 +30,11 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# More hardware work queues than streams in use (main, gather side stream, one
+# per destination rank, NCCL): with the default 8, a stream-memory wait on one
+# queue can stall unrelated streams mapped onto it.  Set before CUDA starts.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
 
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
@@ -225,7 +230,7 @@ def run_gpu(args, world, rank, local):
     # decode of step i + 1; step i + 2 waits for it before reusing the buffer
     outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     out = outs[0]
-    gmode = args.gather if args.gather != "auto" else ("ce" if world == 2 else "nccl")
+    gmode = args.gather if args.gather != "auto" else ("ce" if world <= 4 else "nccl")
     ce = world > 1 and gmode == "ce"
     res = args.sm_reserve if args.sm_reserve >= 0 else min(48, 8 * world if world > 2 else 16)
     res = res if (world > 1 and not ce) else 0
@@ -595,7 +600,7 @@ def main():
                          "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
     ap.add_argument("--gather", default="auto", choices=("auto", "ce", "nccl"),
                     help="N>1 output all-gather: copy engines over NVLink (ce) or NCCL; auto "
-                         "picks the measured faster one (ce at N=2, NCCL + SM reservation at N>=4)")
+                         "picks the measured faster one (ce at N<=4, NCCL + SM reservation at N=8)")
     ap.add_argument("--no-graph", action="store_true",
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
