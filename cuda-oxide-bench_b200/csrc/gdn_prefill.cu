@@ -140,16 +140,10 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int b
 }
 
 // ------------------------------------------------------------ triangular solve
-// m16n8k8 TF32 warp MMA with the 3xTF32 split (hi*hi + hi*lo + lo*hi), which
-// keeps the block products of the solve at close to fp32 accuracy.  hi keeps
-// the top 19 bits of x (exactly representable in tf32) and lo = x - hi is
-// exact in fp32; the tensor core reads only the tf32 bits of lo.  Bit masking
-// keeps the split on the integer pipe.
-__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
-  hi = __float_as_uint(x) & 0xFFFFE000u;
-  lo = __float_as_uint(x - __uint_as_float(hi));
-}
-
+// m16n8k8 TF32 warp MMA for the block products of the solve.  A single TF32
+// product (10-bit mantissa, ~5e-4 relative) is enough: T is rounded to bf16
+// (~4e-3 relative) right after the solve, before any use.  The tensor core
+// reads only the tf32 bits of its fp32 operands.
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
   asm volatile(
       "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
@@ -163,19 +157,17 @@ __device__ __forceinline__ void block_mma(float (&acc)[2][4], const float* x, co
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int ks = 0; ks < 2; ++ks) {
-    uint32_t ah[4], al[4];
-    tf32_split(x[g * kLd + ks * 8 + t], ah[0], al[0]);
-    tf32_split(x[(g + 8) * kLd + ks * 8 + t], ah[1], al[1]);
-    tf32_split(x[g * kLd + ks * 8 + t + 4], ah[2], al[2]);
-    tf32_split(x[(g + 8) * kLd + ks * 8 + t + 4], ah[3], al[3]);
+    uint32_t af[4];
+    af[0] = __float_as_uint(x[g * kLd + ks * 8 + t]);
+    af[1] = __float_as_uint(x[(g + 8) * kLd + ks * 8 + t]);
+    af[2] = __float_as_uint(x[g * kLd + ks * 8 + t + 4]);
+    af[3] = __float_as_uint(x[(g + 8) * kLd + ks * 8 + t + 4]);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      uint32_t bh[2], bl[2];
-      tf32_split(y[(ks * 8 + t) * kLd + nt * 8 + g], bh[0], bl[0]);
-      tf32_split(y[(ks * 8 + t + 4) * kLd + nt * 8 + g], bh[1], bl[1]);
-      mma_tf32(acc[nt], al, bh);
-      mma_tf32(acc[nt], ah, bl);
-      mma_tf32(acc[nt], ah, bh);
+      uint32_t bf[2];
+      bf[0] = __float_as_uint(y[(ks * 8 + t) * kLd + nt * 8 + g]);
+      bf[1] = __float_as_uint(y[(ks * 8 + t + 4) * kLd + nt * 8 + g]);
+      mma_tf32(acc[nt], af, bf);
     }
   }
 }
@@ -195,7 +187,7 @@ __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], 
 // intra warps (warps 0-3 compute; the others only join the group barriers).  Steps: the four 16 x 16 diagonal blocks D_r by
 // forward substitution (one warp each, one lane per column, fp32); T_10 =
 // -D_1 A_10 D_0 and T_32 = -D_3 A_32 D_2; then the lower-left quadrant
-// -T_bot A_bl T_top through Y = A_bl T_top.  Each block of A is last read
+// -T_bot A_bl T_top through Y = A_bl T_top (TF32 warp MMAs).  Each block of A is last read
 // before the block of T that replaces it is written.
 __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, int lane) {
   if (warp < 4) {
