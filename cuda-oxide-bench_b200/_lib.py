@@ -16,7 +16,7 @@ LIB_PATH = _PKG_DIR / "libgdn_b200.so"
 # enums mirrored from include/gdn_b200.h
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 GATE_LOG, GATE_LINEAR = 0, 1
-DECODE_L2NORM_QK, DECODE_GATE_RAW = 1, 2
+DECODE_L2NORM_QK, DECODE_GATE_RAW, DECODE_OUT_NORM_GATE = 1, 2, 4
 OK = 0
 ERR_DEVICE_WAIT = 8
 
@@ -77,6 +77,10 @@ class DecodeArgs(ctypes.Structure):
         ("A_log", ctypes.c_void_p),
         ("dt_bias", ctypes.c_void_p),
         ("state_dtype", ctypes.c_int32),
+        ("z", ctypes.c_void_p),
+        ("z_sb", ctypes.c_int64), ("z_sh", ctypes.c_int64),
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
     ]
 
 

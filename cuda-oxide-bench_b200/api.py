@@ -64,7 +64,8 @@ def _stream_ptr(dev: torch.device) -> int:
 
 def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
                  sm_reserve: int = 0, l2norm_qk: bool = False, l2_eps: float = 1e-6,
-                 A_log=None, dt_bias=None) -> _lib.DecodeArgs:
+                 A_log=None, dt_bias=None, z=None, norm_weight=None,
+                 norm_eps: float = 1e-6) -> _lib.DecodeArgs:
     if q.dim() != 3 or k.shape != q.shape or v.dim() != 3:
         raise GDNError("q, k must be [B, Hqk, d_k] and v [B, Hv, d_v]", 2)
     B, Hqk, dk = q.shape
@@ -126,6 +127,18 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
                 raise GDNError(f"{name} must be a contiguous fp32 [Hv] tensor on {q.device}", 2)
         a.flags |= _lib.DECODE_GATE_RAW
         a.A_log, a.dt_bias = A_log.data_ptr(), dt_bias.data_ptr()
+    if (z is None) != (norm_weight is None):
+        raise GDNError("z and norm_weight go together (output norm/gate)", 1)
+    if z is not None:
+        if tuple(z.shape) != (B, Hv, dv) or z.dtype != q.dtype or z.stride(-1) != 1 \
+                or z.device != q.device:
+            raise GDNError("z must be [B, Hv, d_v] in q's dtype with contiguous rows", 2)
+        if norm_weight.dtype != torch.float32 or tuple(norm_weight.shape) != (dv,) \
+                or not norm_weight.is_contiguous() or norm_weight.device != q.device:
+            raise GDNError("norm_weight must be a contiguous fp32 [d_v] tensor", 2)
+        a.flags |= _lib.DECODE_OUT_NORM_GATE
+        a.z, a.z_sb, a.z_sh = z.data_ptr(), z.stride(0), z.stride(1)
+        a.norm_weight, a.norm_eps = norm_weight.data_ptr(), float(norm_eps)
     return a
 
 
@@ -137,14 +150,16 @@ class DecodeStep:
 
     def __init__(self, q, k, v, g, beta, state, *, out=None, state_out=None, scale=1.0,
                  gate="log", kda=False, sm_reserve=0, l2norm_qk=False, l2_eps=1e-6,
-                 A_log=None, dt_bias=None):
+                 A_log=None, dt_bias=None, z=None, norm_weight=None, norm_eps=1e-6):
         dev = _require_cuda(q, k, v, g, beta, state)
         self.out = out if out is not None else torch.empty(
             (v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
         state_out = state if state_out is None else state_out
-        self._keep = (q, k, v, g, beta, state, state_out, self.out, A_log, dt_bias)
+        self._keep = (q, k, v, g, beta, state, state_out, self.out, A_log, dt_bias, z,
+                      norm_weight)
         self._args = _decode_args(q, k, v, g, beta, state, state_out, self.out, scale, gate, kda,
-                                  sm_reserve, l2norm_qk, l2_eps, A_log, dt_bias)
+                                  sm_reserve, l2norm_qk, l2_eps, A_log, dt_bias, z, norm_weight,
+                                  norm_eps)
         self._argp = ctypes.byref(self._args)
         L = _lib.load()
         self._fn = L.kda_decode_launch if kda else L.gdn_decode_launch
@@ -161,7 +176,7 @@ class DecodeStep:
 def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: str = "log",
                state_out=None, check: bool = False, sm_reserve: int = 0,
                l2norm_qk: bool = False, l2_eps: float = 1e-6, A_log=None,
-               dt_bias=None) -> torch.Tensor:
+               dt_bias=None, z=None, norm_weight=None, norm_eps: float = 1e-6) -> torch.Tensor:
     """One GDN decode step; ``state`` is updated in place (or written to
     ``state_out``).  Returns o [B, Hv, d_v] in q's dtype.
 
@@ -174,14 +189,16 @@ def gdn_decode(q, k, v, g, beta, state, *, scale: float = 1.0, out=None, gate: s
     Fused layer preprocessing: ``l2norm_qk=True`` L2-normalises q and k per
     head inside the kernel (x / sqrt(sum x^2 + l2_eps)); with ``A_log`` and
     ``dt_bias`` ([Hv] fp32) ``g`` is the raw gate projection ``a`` and the log
-    gate is -exp(A_log) * softplus(a + dt_bias).
+    gate is -exp(A_log) * softplus(a + dt_bias); with ``z`` ([B, Hv, d_v]) and
+    ``norm_weight`` ([d_v] fp32) the output becomes
+    RMSNorm(o) * norm_weight * silu(z) per head (d_v in {64, 128}).
     """
     dev = _require_cuda(q, k, v, g, beta, state)
     if out is None:
         out = torch.empty((v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
     so = state if state_out is None else state_out
     a = _decode_args(q, k, v, g, beta, state, so, out, scale, gate, False, sm_reserve,
-                     l2norm_qk, l2_eps, A_log, dt_bias)
+                     l2norm_qk, l2_eps, A_log, dt_bias, z, norm_weight, norm_eps)
     _lib.check(_lib.load().gdn_decode_launch(ctypes.byref(a), _stream_ptr(dev)), "gdn_decode")
     if check:
         check_device_status(dev)

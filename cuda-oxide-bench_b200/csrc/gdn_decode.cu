@@ -208,6 +208,17 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
       }
     }
 
+    // output norm/gate operand z (fused layer step), fetched while the slab lands
+    float zf[4] = {0.f, 0.f, 0.f, 0.f};
+    if (PRE && (a.flags & GDN_DECODE_OUT_NORM_GATE) && rg == 0) {
+      const IO* zp = static_cast<const IO*>(a.z) + b * a.z_sb + static_cast<int64_t>(h) * a.z_sh +
+                     static_cast<int64_t>(vb) * BV + cg * 4;
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(zp));
+      const IO* zv = reinterpret_cast<const IO*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) zf[e] = to_f32(zv[e]);
+    }
+
     // A timed-out thread still runs to the reduction barrier below, where the
     // consumers agree (bar.red.or) to stop together; no thread is left behind
     // on a barrier.
@@ -329,11 +340,28 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
 
     if (rg == 0) {
       const float bqk = beta * qk;
+      float of[4];
+      of[0] = scale * fmaf(bqk, r.x, qs.x);
+      of[1] = scale * fmaf(bqk, r.y, qs.y);
+      of[2] = scale * fmaf(bqk, r.z, qs.z);
+      of[3] = scale * fmaf(bqk, r.w, qs.w);
+      if (PRE && (a.flags & GDN_DECODE_OUT_NORM_GATE)) {
+        // the slab is the whole d_v row (BV == d_v): these kColGroups lanes of
+        // warp 0 hold the head's complete output
+        float ss = of[0] * of[0] + of[1] * of[1] + of[2] * of[2] + of[3] * of[3];
+        constexpr unsigned kMask = Tr::kColGroups == 32 ? 0xffffffffu : ((1u << Tr::kColGroups) - 1u);
+#pragma unroll
+        for (int off = Tr::kColGroups / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(kMask, ss, off);
+        const float rstd = rsqrtf(ss / static_cast<float>(BV) + a.norm_eps);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float silu = zf[e] / (1.f + __expf(-zf[e]));
+          of[e] = of[e] * rstd * __ldg(a.norm_weight + cg * 4 + e) * silu;
+        }
+      }
       IO ov[4];
-      ov[0] = from_f32<IO>(scale * fmaf(bqk, r.x, qs.x));
-      ov[1] = from_f32<IO>(scale * fmaf(bqk, r.y, qs.y));
-      ov[2] = from_f32<IO>(scale * fmaf(bqk, r.z, qs.z));
-      ov[3] = from_f32<IO>(scale * fmaf(bqk, r.w, qs.w));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ov[e] = from_f32<IO>(of[e]);
       IO* o = static_cast<IO*>(a.o) + b * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
               static_cast<int64_t>(vb) * BV + cg * 4;
       *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(ov);
@@ -418,7 +446,14 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
   if (a->io_dtype != GDN_DT_BF16 && a->io_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
   if (!dtype_valid(a->g_dtype) || !dtype_valid(a->beta_dtype)) return GDN_ERR_DTYPE;
   if (a->gate_kind != GDN_GATE_LOG && a->gate_kind != GDN_GATE_LINEAR) return GDN_ERR_DTYPE;
-  if (a->flags & ~(GDN_DECODE_L2NORM_QK | GDN_DECODE_GATE_RAW)) return GDN_ERR_DTYPE;
+  if (a->flags & ~(GDN_DECODE_L2NORM_QK | GDN_DECODE_GATE_RAW | GDN_DECODE_OUT_NORM_GATE))
+    return GDN_ERR_DTYPE;
+  if (a->flags & GDN_DECODE_OUT_NORM_GATE) {
+    if (!a->z || !a->norm_weight) return GDN_ERR_NULL;
+    if ((a->dv != 64 && a->dv != 128) || a->dk > 128 || (a->dk == 64 && a->dv != 64))
+      return GDN_ERR_SHAPE;
+    if (!aligned16(a->z) || !stride_ok(a->z_sb, 2) || !stride_ok(a->z_sh, 2)) return GDN_ERR_ALIGN;
+  }
   if (a->state_dtype != GDN_DT_F32 && a->state_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
   if (a->flags & GDN_DECODE_GATE_RAW) {
     if (kda) return GDN_ERR_DTYPE;  // the raw-gate formula is the scalar GDN gate
@@ -452,6 +487,7 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
 // a single contiguous copy) that still gives every SM at least four slabs;
 // small batches fall back to narrower blocks for balance.
 static int pick_bv(const gdn_decode_args_t& a, int sm_count) {
+  if (a.flags & GDN_DECODE_OUT_NORM_GATE) return a.dv;  // the norm needs whole rows
   static const int kAllowed128[] = {128, 64, 32};
   static const int kAllowed256[] = {64, 32};
   const int* allowed = a.dk == 256 ? kAllowed256 : kAllowed128;

@@ -73,6 +73,9 @@ enum {
   GDN_DECODE_L2NORM_QK = 1u << 0, /* q, k <- x / sqrt(sum x^2 + l2_eps) in-kernel    */
   GDN_DECODE_GATE_RAW = 1u << 1,  /* g is the raw gate projection a:                */
                                   /*   log gate = -exp(A_log[h]) softplus(a + dt_bias[h]) */
+  GDN_DECODE_OUT_NORM_GATE = 1u << 2, /* o <- RMSNorm(o) * norm_weight * silu(z) per  */
+                                      /* (b, h) over d_v; needs d_v in {64, 128},    */
+                                      /* d_k <= 128                                  */
 };
 
 /* device-side status bits (OR-ed into *status) */
@@ -119,6 +122,10 @@ typedef struct {
   int32_t state_dtype;  /* GDN_DT_F32 (default) or GDN_DT_F16 (d_k = 128):   */
                         /* an fp16 state halves the bytes a step streams;    */
                         /* arithmetic stays fp32                             */
+  const void* z;        /* [B, Hv, d_v] io_dtype, with GDN_DECODE_OUT_NORM_GATE */
+  int64_t z_sb, z_sh;   /* element strides of z                              */
+  const float* norm_weight; /* [d_v] fp32 RMSNorm weight                     */
+  float norm_eps;       /* RMSNorm epsilon                                   */
 } gdn_decode_args_t;
 
 /*

@@ -89,6 +89,7 @@ def _valid_args(pkg, **over):
     ({"flags": 8}, 4),           # unknown option bit
     ({"flags": 2}, 1),           # raw gate without A_log / dt_bias
     ({"flags": 1, "l2_eps": -1.0}, 2),
+    ({"flags": 4}, 1),           # output norm/gate without z / norm_weight
 ])
 def test_decode_validation_rejects(pkg, over, code):
     L = pkg._lib.load()

@@ -275,3 +275,39 @@ def test_fp16_state_within_tolerance(pkg, inputs, orc, B, steps):
         np.testing.assert_allclose(o.float().cpu().numpy(), o_ref[t], rtol=O_RTOL, atol=O_ATOL)
     pkg.check_device_status()
     assert np.abs(st.float().cpu().numpy() - s_ref).max() < 2e-3  # fp16-state bound, see docstring
+
+
+def test_fused_layer_step_with_output_norm_gate(pkg, orc):
+    """The whole layer step in one kernel: raw q/k (L2-normalised in-kernel),
+    raw gate projection, and the output gated RMSNorm
+    o <- RMSNorm(o) * w * silu(z) (norm before gate), against the oracle plus
+    the same post-processing in fp32."""
+    import torch.nn.functional as F
+    steps, B, Hqk, Hv, d = 4, 4, 2, 4, 128
+    gen = torch.Generator().manual_seed(77)
+    q = (torch.randn((steps, B, Hqk, d), generator=gen) * 2).to(torch.bfloat16)
+    k = (torch.randn((steps, B, Hqk, d), generator=gen) * 2).to(torch.bfloat16)
+    v = torch.randn((steps, B, Hv, d), generator=gen).to(torch.bfloat16)
+    z = torch.randn((steps, B, Hv, d), generator=gen).to(torch.bfloat16)
+    a = torch.randn((steps, B, Hv), generator=gen)
+    beta = torch.sigmoid(torch.randn((steps, B, Hv), generator=gen))
+    A_log = torch.log(1 + 15 * torch.rand(Hv, generator=gen))
+    dt_bias = -4 + 3 * torch.rand(Hv, generator=gen)
+    w = 0.5 + torch.rand(d, generator=gen)
+    S0 = torch.randn((B, Hv, d, d), generator=gen) * 0.02
+    eps = 1e-6
+    nrm = lambda x: x.float() / torch.sqrt((x.float() ** 2).sum(-1, keepdim=True) + eps)
+    g = -torch.exp(A_log) * F.softplus(a + dt_bias)
+    o_ref, s_ref = orc.gdn_decode_steps(nrm(q), nrm(k), v, g, beta, S0)
+    o_ref = torch.from_numpy(o_ref)
+    rms = torch.rsqrt((o_ref ** 2).mean(-1, keepdim=True) + eps)
+    o_ref = (o_ref * rms * w * F.silu(z.float())).numpy()
+    st = S0.to(DEV)
+    for t in range(steps):
+        o = pkg.gdn_decode(q[t].to(DEV), k[t].to(DEV), v[t].to(DEV), a[t].to(DEV),
+                           beta[t].to(DEV), st, l2norm_qk=True, l2_eps=eps,
+                           A_log=A_log.to(DEV), dt_bias=dt_bias.to(DEV),
+                           z=z[t].to(DEV), norm_weight=w.to(DEV), norm_eps=eps)
+        np.testing.assert_allclose(o.float().cpu().numpy(), o_ref[t], rtol=O_RTOL, atol=O_ATOL)
+    pkg.check_device_status()
+    assert np.abs(st.cpu().numpy() - s_ref).max() < S_ATOL
