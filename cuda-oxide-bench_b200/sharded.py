@@ -224,3 +224,42 @@ class PeerGather:
         for p in self._opened:
             self._lib.gdn_ipc_close(p)
         self._opened = []
+
+
+def gdn_prefill_seqpar(q, k, v, g, beta, initial_state=None, *, group=None, scale: float = 1.0):
+    """Sequence-parallel GDN prefill: rank j of the group holds the j-th
+    contiguous T-segment of every sequence (q, k [B, T_j, Hqk, d], v [B, T_j,
+    Hv, d], g, beta [B, T_j, Hv]) and gets back that segment's outputs plus the
+    state after its segment (on the last rank: the final state).
+
+    The delta-rule recurrence is affine in the state over a segment,
+    S_end = M S_start + L, with M = prod_t a_t (I - beta_t k_t k_t^T) (d_k x d_k)
+    and L the segment's state from zero.  Each rank obtains M by running the
+    chunked prefill from the identity state with v = 0, and L by running it
+    from zero; one all-gather exchanges (M_j, L_j); each rank scans the
+    segment start states in fp32 and re-runs its segment from its start state
+    for exact outputs.  Three prefills of length T/N per rank plus an
+    all-gather of 2 x [B, Hv, d, d] fp32.
+    ``initial_state`` (the state before segment 0) must be given on every rank
+    or on none.
+    """
+    from .api import gdn_prefill
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, T, _, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if dk != dv:
+        raise ValueError("sequence-parallel prefill needs d_k == d_v (M is d_k x d_k)")
+    dev = q.device
+    eye = torch.eye(dk, dtype=torch.float32, device=dev).expand(B, Hv, dk, dk).contiguous()
+    _, M = gdn_prefill(q, k, torch.zeros_like(v), g, beta, eye, scale=scale)
+    _, L = gdn_prefill(q, k, v, g, beta, None, scale=scale)
+    ML = torch.stack([M, L])                                        # [2, B, Hv, d, d]
+    allml = torch.empty((world,) + tuple(ML.shape), dtype=ML.dtype, device=dev)
+    dist.all_gather_into_tensor(allml.view(-1), ML.reshape(-1), group=group)
+    S = (initial_state.float() if initial_state is not None
+         else torch.zeros((B, Hv, dk, dv), dtype=torch.float32, device=dev))
+    for j in range(rank):  # start state of this rank's segment (fp32 matmuls)
+        S = torch.matmul(allml[j, 0], S) + allml[j, 1]
+    o, S_end = gdn_prefill(q, k, v, g, beta, S.contiguous(), scale=scale)
+    return o, S_end

@@ -130,3 +130,46 @@ def test_copy_engine_gather_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert res == {0: True, 1: True}
+
+
+def _seqpar_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        sh = graft.submodule("sharded")
+        inputs = graft.submodule("inputs")
+        p = inputs.make_prefill_inputs(1, 300, 2, 4, 128, seed=9)
+        S0 = torch.randn((1, 4, 128, 128), generator=torch.Generator().manual_seed(3)) * 0.02
+        cut = [0, 128, 300]  # uneven segments, the second one ragged
+        seg = [t[:, cut[rank]:cut[rank + 1]].contiguous().cuda() for t in (p.q, p.k, p.v, p.g, p.beta)]
+        o, S = sh.gdn_prefill_seqpar(*seg, S0.cuda())
+        q.put((rank, o.float().cpu().numpy(), S.cpu().numpy()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_sequence_parallel_prefill_two_gpus():
+    """T split over two GPUs: outputs of both segments and the final state
+    match the sequential recurrence over the whole sequence."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_seqpar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (o, S) for r, o, S in (q.get(timeout=300) for _ in range(2))}
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    inputs = graft.submodule("inputs")
+    p = inputs.make_prefill_inputs(1, 300, 2, 4, 128, seed=9)
+    S0 = torch.randn((1, 4, 128, 128), generator=torch.Generator().manual_seed(3)) * 0.02
+    o_ref, s_ref = graft.oracle().gdn_prefill(p.q, p.k, p.v, p.g, p.beta, S0)
+    o = np.concatenate([res[0][0], res[1][0]], axis=1)
+    np.testing.assert_allclose(o, o_ref, rtol=2e-2, atol=1e-2)
+    assert np.abs(res[1][1] - s_ref).max() < 1e-3
