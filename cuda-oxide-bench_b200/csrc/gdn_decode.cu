@@ -56,7 +56,11 @@ struct DecodeParams {
 // state, which halves the bytes a step streams).
 template <int DK, int BV, bool KDA, int SB = 4>
 struct DecodeTraits {
-  static constexpr int kConsumerWarps = 8;
+  // Small-batch variant (32-column slabs, d_k <= 128): 4 consumer warps and 4
+  // CTAs per SM, so a small step's few slabs per SM run side by side instead of
+  // one after another.
+  static constexpr bool kSmall = BV == 32 && DK <= 128;
+  static constexpr int kConsumerWarps = kSmall ? 4 : 8;
   static constexpr int kConsumers = kConsumerWarps * 32;
   static constexpr int kThreads = kConsumers + 32;
   static constexpr int kColGroups = BV / 4;                  // float4 columns
@@ -65,8 +69,8 @@ struct DecodeTraits {
   static constexpr int kMaxStages = 8;
   // Narrow (32-column) slabs come with small batches, where a CTA walks a few
   // slabs back to back and each slab's reduction latency is exposed: those
-  // variants run two CTAs per SM (fewer registers, half the smem ring each).
-  static constexpr int kCtasPerSm = BV == 32 ? 2 : 1;
+  // variants run several CTAs per SM (fewer registers, a share of the smem).
+  static constexpr int kCtasPerSm = kSmall ? 4 : (BV == 32 ? 2 : 1);
   static constexpr uint32_t kSlabBytes = DK * BV * SB;
   static constexpr uint32_t kQKBytes = DK * 2;
   static constexpr uint32_t kVBytes = BV * 2;
