@@ -545,6 +545,27 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
                                           "chunked_form_GFLOP": round(fl / 1e9, 2)}
     except Exception as e:  # prefill not available yet
         ex["config3_prefill_B4_T4096"] = {"unavailable": str(e)[:200]}
+    # KDA prefill (recurrent form, state on chip) at the config 3 length, H=32
+    p = inputs.make_kda_prefill_inputs(4, 4096, 32, 32, D, seed=3, device=dev)
+    fs = torch.empty((4, 32, D, D), dtype=torch.float32, device=dev)
+    po = torch.empty((4, 4096, 32, D), dtype=torch.bfloat16, device=dev)
+    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+    for _ in range(2):
+        fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(5):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 5
+    ex["kda_prefill_B4_T4096_H32"] = {
+        "ms": round(ms, 4), "tokens_per_s": round(4 * 4096 / (ms * 1e-3), 1),
+        "fp32_TOPs_recurrent": round(inputs.kda_recurrent_ops(4, 4096, 32, D) / (ms * 1e-3) / 1e12, 2),
+        "GBps_compulsory": round(inputs.kda_prefill_bytes(4, 4096, 32, 32, D) / (ms * 1e-3) / 1e9, 1),
+        "note": "recurrent form on CUDA cores; no tensor cores"}
+    del p, fs, po
     return ex
 
 

@@ -5,6 +5,7 @@ Entry points (all on CUDA tensors, all through the C ABI of libgdn_b200.so):
 * :func:`gdn_decode` — one GDN decode step, state updated in place.
 * :func:`kda_decode` — one KDA (per-channel gate) decode step.
 * :func:`gdn_prefill` — chunked prefill over T tokens (tcgen05 tensor cores).
+* :func:`kda_prefill` — KDA prefill over T tokens (state kept on chip).
 * :func:`gdn_decode_ref` / :func:`kda_decode_ref` — the reference's 2-D
   (Q, K, V, Alpha|G, Beta, S_in, S_out, O) argument layout.
 * :class:`ShardedGDNDecoder` — value-head-sharded decode over several GPUs
@@ -21,6 +22,7 @@ from .api import (
     gdn_decode_ref,
     gdn_prefill,
     kda_decode,
+    kda_prefill,
     kda_decode_ref,
     status_word,
 )
@@ -28,6 +30,6 @@ from .sharded import ShardedGDNDecoder, shard_heads
 
 __all__ = [
     "GDNError", "LIB_PATH", "DecodeStep", "check_device_status", "gdn_decode",
-    "gdn_decode_ref", "gdn_prefill", "kda_decode", "kda_decode_ref", "status_word",
+    "gdn_decode_ref", "gdn_prefill", "kda_decode", "kda_prefill", "kda_decode_ref", "status_word",
     "ShardedGDNDecoder", "shard_heads",
 ]

@@ -37,6 +37,7 @@ EXPORTED = (
     "kda_decode_ref_launch",
     "gdn_prefill_workspace_size",
     "gdn_prefill_launch",
+    "kda_prefill_launch",
     "gdn_ipc_handle",
     "gdn_ipc_open",
     "gdn_ipc_close",
@@ -135,6 +136,8 @@ def load(path: str | Path | None = None):
         L.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         L.gdn_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
         L.gdn_prefill_launch.restype = ctypes.c_int
+        L.kda_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
+        L.kda_prefill_launch.restype = ctypes.c_int
         L.gdn_ipc_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
         L.gdn_ipc_open.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
         L.gdn_ipc_close.argtypes = [vp]

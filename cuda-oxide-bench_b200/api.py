@@ -255,13 +255,15 @@ def kda_decode_ref(Q, K, V, G, Beta, S_in, S_out, O, *, batch: int, n_heads: int
     _lib.check(rc, "kda_decode_ref")
 
 
-def _prefill_args(q, k, v, g, beta, initial_state, final_state, o, chunk, scale):
+def _prefill_args(q, k, v, g, beta, initial_state, final_state, o, chunk, scale, kda=False):
     if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
         raise GDNError("q, k must be [B, T, Hqk, d_k] and v [B, T, Hv, d_v]", 2)
     B, T, Hqk, dk = q.shape
     Hv, dv = v.shape[2], v.shape[3]
-    if tuple(v.shape[:2]) != (B, T) or tuple(g.shape) != (B, T, Hv) or tuple(beta.shape) != (B, T, Hv):
-        raise GDNError("v [B,T,Hv,d_v], g and beta [B,T,Hv] must match q [B,T,Hqk,d_k]", 2)
+    g_shape = (B, T, Hv, dk) if kda else (B, T, Hv)
+    if tuple(v.shape[:2]) != (B, T) or tuple(g.shape) != g_shape or tuple(beta.shape) != (B, T, Hv):
+        raise GDNError(f"v [B,T,Hv,d_v], g {'[B,T,Hv,d_k]' if kda else '[B,T,Hv]'} and beta "
+                       "[B,T,Hv] must match q [B,T,Hqk,d_k]", 2)
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta), ("out", o)):
         if not t.is_contiguous():
             raise GDNError(f"{name} must be contiguous", 3)
@@ -310,6 +312,28 @@ def gdn_prefill(q, k, v, g, beta, initial_state=None, *, chunk_size: int = 64,
             workspace = ws
         a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     _lib.check(L.gdn_prefill_launch(ctypes.byref(a), _stream_ptr(dev)), "gdn_prefill")
+    if check:
+        check_device_status(dev)
+    return out, final_state
+
+
+def kda_prefill(q, k, v, g, beta, initial_state=None, *, scale: float = 1.0, out=None,
+                final_state=None, check: bool = False):
+    """KDA prefill over T tokens: T applications of the reference's
+    naive_recurrent_kda_step (pytorch_reference_kda.py:42-71) with the state
+    threaded through.  q, k [B,T,Hqk,d_k]; v [B,T,Hv,d_v]; g [B,T,Hv,d_k]
+    per-channel log gate; beta [B,T,Hv].  Returns (o [B,T,Hv,d_v],
+    final_state fp32 [B,Hv,d_k,d_v]).  ``final_state`` may be the
+    ``initial_state`` tensor (updated in place)."""
+    dev = _require_cuda(q, k, v, g, beta)
+    B, T, _, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if out is None:
+        out = torch.empty((B, T, Hv, dv), dtype=q.dtype, device=dev)
+    if final_state is None:
+        final_state = torch.empty((B, Hv, dk, dv), dtype=torch.float32, device=dev)
+    a = _prefill_args(q, k, v, g, beta, initial_state, final_state, out, 0, scale, kda=True)
+    _lib.check(_lib.load().kda_prefill_launch(ctypes.byref(a), _stream_ptr(dev)), "kda_prefill")
     if check:
         check_device_status(dev)
     return out, final_state

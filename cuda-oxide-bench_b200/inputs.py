@@ -97,6 +97,37 @@ def make_prefill_inputs(B: int, T: int, Hqk: int, Hv: int, d: int = 128, *, seed
     return PrefillInputs(q, k, v, g, beta)
 
 
+def make_kda_prefill_inputs(B: int, T: int, Hqk: int, Hv: int, d: int = 128, *, seed: int = 0,
+                            device="cpu", io_dtype=torch.bfloat16,
+                            g_dtype=torch.float32) -> PrefillInputs:
+    """KDA prefill: the config 2 distributions drawn per token, g [B,T,Hv,d]."""
+    gen = _gen(seed, device)
+    q = _l2norm(torch.randn((B, T, Hqk, d), generator=gen, device=device)).to(io_dtype)
+    k = _l2norm(torch.randn((B, T, Hqk, d), generator=gen, device=device)).to(io_dtype)
+    v = torch.randn((B, T, Hv, d), generator=gen, device=device).to(io_dtype)
+    beta = torch.sigmoid(torch.randn((B, T, Hv), generator=gen, device=device)).to(io_dtype)
+    n = torch.randn((B, T, Hv, d), generator=gen, device=device)
+    u = -5.0 * torch.rand((B, T, Hv, d), generator=gen, device=device)
+    g = (-F.softplus(n) * torch.exp(u)).to(g_dtype)
+    return PrefillInputs(q, k, v, g, beta)
+
+
+def kda_prefill_bytes(B: int, T: int, Hqk: int, Hv: int, d: int = 128, io_bytes: int = 2,
+                      g_bytes: int = 4) -> int:
+    """Compulsory HBM bytes: q, k, v, g, beta read once, o and the final state
+    written once (zero initial state)."""
+    tok = B * T
+    return tok * (2 * Hqk * d * io_bytes + Hv * d * io_bytes * 2 + Hv * d * g_bytes
+                  + Hv * io_bytes) + B * Hv * d * d * 4
+
+
+def kda_recurrent_ops(B: int, T: int, Hv: int, d: int = 128) -> int:
+    """fp32 operations of the recurrent form: per token and head, the decay,
+    the two column sums and the rank-1 update, d*d each (FMA counted as 2
+    except the decay multiply)."""
+    return B * T * Hv * d * d * 7
+
+
 # Algorithmic bytes / FLOPs (the numerators of every roofline figure).
 
 def gdn_decode_bytes(B: int, Hqk: int, Hv: int, dk: int = 128, dv: int = 128,

@@ -215,6 +215,18 @@ size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args);
  */
 int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
+/*
+ * KDA prefill: T applications of the reference's per-channel-gate step
+ * naive_recurrent_kda_step
+ * (analysis/wave15-attention-architecture/reference/pytorch_reference_kda.py:42-71),
+ * which the reference only runs one token at a time.  Same argument struct as
+ * gdn_prefill_launch, except that g is the per-channel log gate
+ * [B, T, Hv, d_k] (g_dtype) and chunk is ignored.  d_k, d_v in {64, 128, 256};
+ * g 16-byte aligned, beta and the states 4-byte aligned.  initial_state may
+ * equal final_state (updated in place).  No workspace.
+ */
+int kda_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Multi-GPU: all-gather of per-rank decode outputs with the copy engines.
  * The reference is single-GPU (METHODOLOGY.md:80); these entry points have no

@@ -174,3 +174,18 @@ def gdn_prefill(q, k, v, g, beta, S0=None, *, scale=1.0):
 
 if __name__ == "__main__":
     print(build(force=True), "threads:", num_threads())
+
+
+def kda_prefill(q, k, v, g, beta, S0=None, *, scale=1.0):
+    """KDA prefill oracle: T applications of the reference KDA step
+    (naive_recurrent_kda_step, pytorch_reference_kda.py:42-71) in float64.
+
+    q, k [B,T,Hqk,dk]; v [B,T,Hv,dv]; g [B,T,Hv,dk]; beta [B,T,Hv];
+    S0 [B,Hv,dk,dv] or None.  Returns (o [B,T,Hv,dv] f64, S_final f64).
+    """
+    tm = lambda x: np.ascontiguousarray(np.swapaxes(_f32(x), 0, 1))  # [B,T,..] -> [T,B,..]
+    q, k, v, g, beta = map(tm, (q, k, v, g, beta))
+    B, Hv, dk, dv = q.shape[1], v.shape[2], q.shape[3], v.shape[3]
+    S = np.zeros((B, Hv, dk, dv)) if S0 is None else S0
+    o, S = kda_decode_steps(q, k, v, g, beta, S, scale=scale)
+    return np.ascontiguousarray(np.swapaxes(o, 0, 1)), S

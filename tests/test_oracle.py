@@ -110,3 +110,21 @@ def test_input_distributions(inputs):
     assert abs(float(x.state.std()) - 0.02) < 1e-3
     y = inputs.make_decode_inputs(1, 2, 4, 4, 128, kda=True, seed=0)
     assert y.g.shape == (1, 2, 4, 128) and bool((y.g < 0).all())
+
+
+def test_kda_prefill_oracle_equals_numpy_steps(orc, inputs):
+    """The KDA prefill oracle (C, float64) equals the numpy restatement of the
+    reference step applied token by token."""
+    p = inputs.make_kda_prefill_inputs(2, 5, 1, 2, 16, seed=9)
+    S0 = np.random.default_rng(0).normal(0, 0.02, (2, 2, 16, 16))
+    o, S = orc.kda_prefill(p.q, p.k, p.v, p.g, p.beta, S0.copy(), scale=0.5)
+    f = lambda t: t.float().numpy().astype(np.float64)
+    q, k, v, g, beta = map(f, (p.q, p.k, p.v, p.g, p.beta))
+    q = np.repeat(q, 2, axis=2)  # Hqk 1 -> Hv 2 (v head h uses qk head h // 2)
+    k = np.repeat(k, 2, axis=2)
+    Sn = S0.copy()
+    for t in range(5):
+        ot, Sn = orc.kda_decode_step_np(q[:, t], k[:, t], v[:, t], g[:, t], beta[:, t], Sn,
+                                        scale=0.5)
+        assert np.abs(ot - o[:, t]).max() < 1e-9
+    assert np.abs(Sn - S).max() < 1e-9
