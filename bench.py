@@ -606,6 +606,39 @@ def run_prefill(args, world, rank, local):
               flush=True)
 
 
+def run_kda_prefill(args, world, rank, local):
+    """KDA prefill (per-channel gate) at B=4, H=32, T=--seq (default 4096, the
+    config 3 length) as its own line, device-timed; used for profiling."""
+    pkg = graft.package()
+    inputs = graft.submodule("inputs")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    Bp, Tp, H = 4, args.seq, 32
+    p = inputs.make_kda_prefill_inputs(Bp, Tp, H, H, D, seed=3, device=dev)
+    fs = torch.empty((Bp, H, D, D), dtype=torch.float32, device=dev)
+    po = torch.empty((Bp, Tp, H, D), dtype=torch.bfloat16, device=dev)
+    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+    for _ in range(args.warmup):
+        fn()
+    pkg.check_device_status(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.steps
+    if rank == 0:
+        print(json.dumps({"metric": "KDA prefill tokens/s", "value": round(Bp * Tp / (ms * 1e-3), 1),
+                          "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": args.steps,
+                          "warmup": args.warmup, "n_gpus": world,
+                          "fp32_TOPs_recurrent": round(
+                              inputs.kda_recurrent_ops(Bp, Tp, H, D) / (ms * 1e-3) / 1e12, 2),
+                          "config": {"workload": f"KDA prefill B={Bp} T={Tp} H={H} d={D}"}}),
+              flush=True)
+
+
 def main():
     global B
     ap = argparse.ArgumentParser()
@@ -626,8 +659,10 @@ def main():
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="N>1: run each step's all-gather after its decode, not overlapped")
-    ap.add_argument("--workload", default="decode", choices=("decode", "prefill"),
-                    help="decode (headline, configs[1]/4) or prefill (config 3, for profiling)")
+    ap.add_argument("--workload", default="decode", choices=("decode", "prefill", "kda_prefill"),
+                    help="decode (headline, configs[1]/4), prefill (config 3) or kda_prefill "
+                         "(B=4, H=32, T=--seq); the last two for profiling")
+    ap.add_argument("--seq", type=int, default=4096, help="kda_prefill sequence length")
     ap.add_argument("--batch", type=int, default=B,
                     help="decode batch (default 1024, the headline; smaller for ncu captures)")
     args = ap.parse_args()
@@ -641,6 +676,9 @@ def main():
         elif args.workload == "prefill":
             graft.build()
             run_prefill(args, world, rank, local)
+        elif args.workload == "kda_prefill":
+            graft.build()
+            run_kda_prefill(args, world, rank, local)
         else:
             graft.build()
             run_gpu(args, world, rank, local)

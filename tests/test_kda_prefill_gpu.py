@@ -84,3 +84,23 @@ def test_kda_prefill_rejects_bad_args(pkg, inputs):
     q, k, v, g, beta = _dev(p)
     with pytest.raises(pkg.GDNError):
         pkg.kda_prefill(q, k, v, g[..., 0].contiguous(), beta)  # a GDN (per-head) gate
+
+
+@pytest.mark.parametrize("kind", ["strong", "underflow"])
+def test_kda_prefill_extreme_gates(pkg, inputs, orc, kind):
+    """Gates far outside the config distribution: strong decay (g down to -30
+    per token) and gates whose exp() underflows to zero (g = -200).  The
+    kernel's rescaled state must renormalise mid-chunk and stay finite."""
+    p = inputs.make_kda_prefill_inputs(2, 70, 2, 2, 128, seed=31)
+    gen = torch.Generator().manual_seed(7)
+    if kind == "strong":
+        g = -30.0 * torch.rand(p.g.shape, generator=gen)
+    else:
+        g = torch.where(torch.rand(p.g.shape, generator=gen) < 0.1, -200.0, -0.05)
+    S0 = _state(2, 2, 128)
+    o_ref, s_ref = orc.kda_prefill(p.q, p.k, p.v, g, p.beta, S0.double().numpy())
+    o, S = pkg.kda_prefill(p.q.to(DEV), p.k.to(DEV), p.v.to(DEV), g.to(DEV), p.beta.to(DEV),
+                           S0.to(DEV), check=True)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(S).all()
+    np.testing.assert_allclose(o.float().cpu().numpy(), o_ref, rtol=O_RTOL, atol=O_ATOL)
+    assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
