@@ -448,7 +448,10 @@ __global__ void __launch_bounds__(kThreads, DK == 256 ? 1 : 2)
     const float* V = sV + bs * kTC * kBV;
     const float* BQK = sBQK + bs * kTC;
     const uint32_t o_addr0 = smem_u32(sO + bs * kTC * kBV + colw);
-    for (int t = 0; t < n; ++t) {
+    // fully unrolled: every per-token offset and mask bit becomes an immediate
+#pragma unroll
+    for (int t = 0; t < kTC; ++t) {
+      if (t >= n) break;
       if ((mask >> t) & 1u) {  // segment start: S~ <- diag(R) S~
         uint64_t r2[Tr::kP];
         load_pairs(E + t * DK, r2);
