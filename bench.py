@@ -56,16 +56,12 @@ def peaks():
     return HBM_FALLBACK_GBS, BF16_FALLBACK_TFLOPS, "fallback"
 
 
-def profiled_traffic(name: str):
-    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<name>.md,
-    line 'traffic_bytes_per_launch: N'), or None."""
-    f = ROOT / "profiles" / f"{name}.md"
-    if not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            return int(float(line.split(":", 1)[1]))
-    return None
+# DRAM traffic of one headline decode launch (B=1024), from an ncu capture:
+# dram__bytes_read.sum + dram__bytes_write.sum of decode_kernel at B=256
+# (1,021.9 MB; the full B=1024 launch is too large to capture under the
+# profiling size rule), scaled x4 by the sequences processed.  The capture
+# command and its figures are in profiles/gdn_decode_B1024.md.
+DECODE_TRAFFIC_BYTES_B1024 = 4_087_588_352
 
 
 class ClockSampler:
@@ -372,53 +368,35 @@ def run_gpu(args, world, rank, local):
     hbm, bf16, peak_kind = peaks()
     achieved = local_bytes / (kern_ms * 1e-3) / 1e9
 
+    # ---- parity of one more step (and of its gather) against the C oracle
+    def gathered(i):  # [N, B, hv, d] rank-major slot holding step i's gathered outputs
+        if ce:
+            return pg.buf[gstep[0] % 2].view(world, B, hv, D)
+        return gbufs[i % 2]
+
+    parity = decode_parity(graft.oracle(), toks, state, outs, launch, gather, settle, join,
+                           gathered, shard, world, rank, dev)
+
     # ---- e2e through the public API with pinned host buffers
     e2e_steps = min(args.steps, 200)
-    host = [[t.cpu().pin_memory() for t in tk] for tk in toks]
-    dev_in = toks  # the bound device buffers the DecodeSteps read
-    o_host = torch.empty((B, HV if world > 1 else hv, D), dtype=torch.bfloat16).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host[0])
-    d2h = o_host.numel() * o_host.element_size() if (world == 1 or rank == 0) else 0
-    full_o = torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
-
-    def e2e_step(i):
-        j = i % pool
-        for hsrc, ddst in zip(host[j], dev_in[j]):
-            ddst.copy_(hsrc, non_blocking=True)
-        steps[j]()
-        if world > 1:
-            dist.all_gather_into_tensor(gather_buf.view(-1), out.view(-1))
-            full_o.view(B, world, hv, D).copy_(gather_buf.permute(1, 0, 2, 3))
-            if rank == 0:
-                o_host.copy_(full_o, non_blocking=True)
-        else:
-            o_host.copy_(out, non_blocking=True)
-
-    for i in range(3):
-        e2e_step(i)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    f1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world, dev)
+    e2e_ms, h2d, d2h = run_e2e(pkg, toks, state, hv, world, rank, dev, e2e_steps)
     e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
 
     extras = {}
     cpu = None
-    if world == 1 and not args.no_extras:
-        extras = run_extras(pkg, inputs, dev, hbm, bf16)
+    if not args.no_extras:
+        if world == 1:
+            extras = run_extras(pkg, inputs, dev, hbm, bf16, with_cpu=not args.no_cpu)
+        else:
+            extras = run_seqpar_extras(pkg, inputs, dev, world, rank, bf16)
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, cores, sample = cpu_sample(args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": sample}
     if rank != 0:
         return
-    traffic = profiled_traffic(f"gdn_decode_B{B}")
+    # per launch: a rank streams 1/N of the heads, so 1/N of the B=1024 traffic
+    traffic = DECODE_TRAFFIC_BYTES_B1024 // world if B == 1024 else None
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": timed_steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -439,7 +417,11 @@ def run_gpu(args, world, rank, local):
                      "kernel": "decode_kernel<128,128,bf16,GDN>",
                      "algorithmic_bytes_per_launch": local_bytes},
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "copies": "pinned host <-> device every step, double-buffered on two copy "
+                          "streams (H2D of step i+1 and D2H of step i overlap decode); "
+                          "h2d counts all ranks, d2h is rank 0's gathered output"},
+        "parity": parity,
         "gpu_launches": timed_steps,
         "cuda_graph": graph is not None,
         "allgather_overlapped": world > 1 and not args.no_overlap,
@@ -450,6 +432,131 @@ def run_gpu(args, world, rank, local):
         "extras": extras,
     }
     print(json.dumps(line), flush=True)
+
+
+def decode_parity(orc, toks, state, outs, launch, gather, settle, join, gathered, shard,
+                  world, rank, dev, n_seq=8):
+    """One more decode step after the timed region, through the same launch
+    and gather path as the timed steps, checked against the C oracle (the
+    restatement of gdn_decode_reference, pytorch_reference_gdn.py:38-91) on
+    a fixed sample of ``n_seq`` sequences x every local value head: this
+    rank's outputs and state rows, and on rank 0 the gathered [B, Hv, d]
+    rows of every rank's heads.  Tolerances: outputs rtol 2e-2 / atol 1e-2,
+    state max-abs 1e-3."""
+    import numpy as np
+    rtol, atol, s_atol = 2e-2, 1e-2, 1e-3
+    torch.cuda.synchronize(dev)
+    idx = torch.linspace(0, B - 1, n_seq).round().long().to(dev)
+    q, k, v, g, beta = [t.index_select(0, idx).float().cpu() for t in toks[0]]
+    S0 = state.index_select(0, idx).cpu().numpy()
+    launch(0)          # bound to toks[0] and outs[0]
+    gather(0)
+    settle(0)
+    join()
+    torch.cuda.synchronize(dev)
+    o_dev = outs[0].index_select(0, idx).float().cpu().numpy()
+    S1 = state.index_select(0, idx).cpu().numpy()
+    o_ref, s_ref = orc.gdn_decode_steps(q[None], k[None], v[None], g[None], beta[None], S0)
+    o_ref = o_ref[0]
+
+    def excess(x, r):  # > 0 where |x - r| exceeds atol + rtol |r|
+        return float((np.abs(x - r) - (atol + rtol * np.abs(r))).max())
+
+    err_o = float(np.abs(o_dev - o_ref).max())
+    err_s = float(np.abs(S1 - s_ref).max())
+    bad = max(excess(o_dev, o_ref), err_s - s_atol)
+    err_g = None
+    if world > 1:
+        mine = torch.from_numpy(o_ref).to(dev)                       # [n, hv, d]
+        allref = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=dev)
+        dist.all_gather_into_tensor(allref.view(-1), mine.reshape(-1))
+        hv = mine.shape[1]
+        ref_full = allref.permute(1, 0, 2, 3).reshape(n_seq, world * hv, -1).cpu().numpy()
+        got = gathered(0).index_select(1, idx)                       # [N, n, hv, d]
+        got_full = got.permute(1, 0, 2, 3).reshape(n_seq, world * hv, -1).float().cpu().numpy()
+        err_g = float(np.abs(got_full - ref_full).max())
+        bad = max(bad, excess(got_full, ref_full))
+        t = torch.tensor([err_o, err_s, bad], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        err_o, err_s, bad = (float(x) for x in t.tolist())
+    return {"checked": True, "oracle": "C restatement of gdn_decode_reference (fp32)",
+            "sample": f"{n_seq} sequences x all {shard.h1 - shard.h0} local value heads per rank"
+                      + (", gathered rows on rank 0" if world > 1 else ""),
+            "max_abs_o": err_o, "max_abs_S": err_s, "max_abs_o_gathered": err_g,
+            "tol": {"o_rtol": rtol, "o_atol": atol, "S_atol": s_atol}, "ok": bad <= 0.0}
+
+
+def run_e2e(pkg, toks, state, hv, world, rank, dev, n_steps):
+    """End-to-end decode through the public API (DecodeStep; with N > 1 the
+    NCCL all-gather and head-major permute of ShardedGDNDecoder.gather) with
+    host buffers.  Every step copies its q/k/v/g/beta from pinned host memory
+    and reads its output back (rank 0 reads the gathered [B, Hv, d]).  The
+    copies are double-buffered on two copy streams: step i+1's inputs travel
+    while step i decodes, and step i's output travels while step i+1 decodes.
+    Returns (ms per step, max over ranks; H2D bytes per step over all ranks;
+    D2H bytes per step)."""
+    pool = len(toks)
+    host = [[t.cpu().pin_memory() for t in tk] for tk in toks]
+    dev_in = [[torch.empty_like(t) for t in toks[0]] for _ in range(2)]
+    outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    steps = [pkg.DecodeStep(*dev_in[s], state, out=outs[s]) for s in range(2)]
+    reads = world == 1 or rank == 0
+    o_host = [torch.empty((B, HV if world > 1 else hv, D), dtype=torch.bfloat16).pin_memory()
+              for _ in range(2)]
+    full = [torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev) for _ in range(2)] \
+        if world > 1 else None
+    gbuf = torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    comp = torch.cuda.current_stream(dev)
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [None, None]   # step i's decode (and gather) done with dev_in[s], outs[s]
+    ev_read = [None, None]   # step i's output copied to the host
+
+    def step(i):
+        s = i % 2
+        if ev_used[s] is not None:
+            h2d_s.wait_event(ev_used[s])
+        with torch.cuda.stream(h2d_s):
+            for hsrc, ddst in zip(host[i % pool], dev_in[s]):
+                ddst.copy_(hsrc, non_blocking=True)
+        ev_in[s].record(h2d_s)
+        comp.wait_event(ev_in[s])
+        if ev_read[s] is not None:
+            comp.wait_event(ev_read[s])
+        res = steps[s]()
+        if world > 1:
+            dist.all_gather_into_tensor(gbuf.view(-1), res.view(-1))
+            full[s].view(B, world, hv, D).copy_(gbuf.permute(1, 0, 2, 3))
+            res = full[s]
+        ev = torch.cuda.Event()
+        ev.record(comp)
+        ev_used[s] = ev
+        if reads:
+            d2h_s.wait_event(ev)
+            with torch.cuda.stream(d2h_s):
+                o_host[s].copy_(res, non_blocking=True)
+            ev2 = torch.cuda.Event()
+            ev2.record(d2h_s)
+            ev_read[s] = ev2
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(comp)
+    h2d_s.wait_event(f0)
+    for i in range(n_steps):
+        step(i)
+    comp.wait_stream(d2h_s)
+    comp.wait_stream(h2d_s)
+    f1.record(comp)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(f0.elapsed_time(f1) / n_steps, world, dev)
+    h2d = sum(t.numel() * t.element_size() for t in host[0]) * world
+    d2h = o_host[0].numel() * o_host[0].element_size()
+    return ms, h2d, d2h
 
 
 def _time_graph(fn, reps=20, warm=3):
@@ -475,9 +582,73 @@ def _time_graph(fn, reps=20, warm=3):
     return a.elapsed_time(b) / reps
 
 
-def run_extras(pkg, inputs, dev, hbm, bf16):
-    """Secondary BASELINE configs, device-timed (not the headline)."""
+def _cpu_timed(fn, min_seconds=1.0):
+    """Runs fn() once to warm, then repeats it for at least ``min_seconds``;
+    returns seconds per call."""
+    fn()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return el / n
+
+
+def cpu_baselines(inputs):
+    """The oracle port (C, all host threads) timed on bounded samples of the
+    secondary configs; each entry becomes the ``cpu_baseline`` of the matching
+    extras line.  Returns {name: cpu_baseline dict}."""
+    orc = graft.oracle()
+    cores = orc.num_threads()
+    out = {}
+    # config 0: all 64 steps at B=8 (the whole config)
+    x = inputs.make_decode_inputs(64, 8, HQK, HV, D, seed=0)
+    a = [t.float().numpy() for t in (x.q, x.k, x.v, x.g, x.beta)]
+    el = _cpu_timed(lambda: orc.gdn_decode_steps(*a, x.state.numpy()))
+    out["config0"] = {"value": round(8 * 64 / el, 1), "unit": "tokens/s", "cores": cores,
+                      "kind": "port", "sample": "the whole config: 64 steps at B=8, 32 heads",
+                      "seconds": round(el, 3)}
+    # config 1: one step at B=64 (whole) and a B=64 sample of B=256
+    x = inputs.make_decode_inputs(1, 64, HQK, HV, D, seed=1)
+    a = [t.float().numpy() for t in (x.q, x.k, x.v, x.g, x.beta)]
+    el = _cpu_timed(lambda: orc.gdn_decode_steps(*a, x.state.numpy()))
+    gbs = inputs.gdn_decode_bytes(64, HQK, HV) / el / 1e9
+    for b_ in (64, 256):
+        out[f"config1_B{b_}"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+                                 "kind": "port",
+                                 "sample": "one decode step at B=64" + (" (of 256)" if b_ > 64 else ""),
+                                 "seconds": round(el, 3)}
+    # config 2: the whole config, 64 float64 KDA steps at B=64
+    x = inputs.make_decode_inputs(64, 64, 32, 32, D, kda=True, seed=2)
+    a = [t.float().numpy() for t in (x.q, x.k, x.v, x.g, x.beta)]
+    el = _cpu_timed(lambda: orc.kda_decode_steps(*a, x.state.numpy()))
+    out["config2"] = {"value": round(64 * inputs.kda_decode_bytes(64, 32, 32) / el / 1e9, 3),
+                      "unit": "GB/s", "cores": cores, "kind": "port",
+                      "sample": "the whole config: 64 steps at B=64, 32 heads, float64",
+                      "seconds": round(el, 3)}
+    # config 3: the sequential T=4096 recurrence for 16 value heads of one sequence
+    p = inputs.make_prefill_inputs(1, 4096, 8, 16, D, seed=3)
+    el = _cpu_timed(lambda: orc.gdn_prefill(p.q, p.k, p.v, p.g, p.beta))
+    fl = inputs.gdn_prefill_flops(1, 4096, 8, 16, D, 64)
+    out["config3"] = {"value": round(fl / el / 1e12, 5), "unit": "TFLOP/s (chunked-form equivalent)",
+                      "head_tokens_per_s": round(16 * 4096 / el, 1), "cores": cores, "kind": "port",
+                      "sample": "sequential recurrence over T=4096 for b=0, 16 value heads "
+                                "(8 q/k heads) of the 4 x 32", "seconds": round(el, 3)}
+    # KDA prefill: float64 recurrence over T=4096 for 8 heads of one sequence
+    p = inputs.make_kda_prefill_inputs(1, 4096, 8, 8, D, seed=3)
+    el = _cpu_timed(lambda: orc.kda_prefill(p.q, p.k, p.v, p.g, p.beta))
+    out["kda_prefill"] = {"value": round(8 * 4096 / el, 1), "unit": "head-tokens/s", "cores": cores,
+                          "kind": "port", "sample": "float64 recurrence over T=4096 for b=0, "
+                                                    "8 of the 4 x 32 heads", "seconds": round(el, 3)}
+    return out
+
+
+def run_extras(pkg, inputs, dev, hbm, bf16, with_cpu=True):
+    """Secondary BASELINE configs, device-timed (not the headline), each with
+    the CPU oracle port timed beside it on a stated sample."""
     ex = {}
+    cpu = cpu_baselines(inputs) if with_cpu else {}
     # config 0: B=8, 64 sequential steps per CUDA-graph replay
     x = inputs.make_decode_inputs(64, 8, HQK, HV, D, seed=0, device=dev)
     st = x.state.clone()
@@ -487,7 +658,8 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
     ex["config0_gdn_B8_64steps"] = {
         "tokens_per_s": round(8 * 64 / (ms * 1e-3), 1), "us_per_step": round(ms * 1e3 / 64, 3),
         "state_GBps_equiv": round(64 * inputs.gdn_decode_bytes(8, HQK, HV) / (ms * 1e-3) / 1e9, 1),
-        "note": "16.8 MB state is L2-resident; GB/s-equivalent can exceed HBM peak"}
+        "note": "16.8 MB state is L2-resident; GB/s-equivalent can exceed HBM peak",
+        "cpu_baseline": cpu.get("config0")}
     del x, st, s0
     # config 1 sweep (B=64, 256): one step per replay, state in place
     for b in (64, 256):
@@ -497,8 +669,31 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
         ms = _time_graph(lambda: s1(), reps=100)
         gbs = inputs.gdn_decode_bytes(b, HQK, HV) / (ms * 1e-3) / 1e9
         ex[f"config1_gdn_B{b}"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
-                                   "us": round(ms * 1e3, 2)}
+                                   "us": round(ms * 1e3, 2), "cpu_baseline": cpu.get(f"config1_B{b}")}
         del x, st, s1
+    # sustained headline decode: >= 1 s of back-to-back steps, clocks sampled
+    x = inputs.make_decode_inputs(1, B, HQK, HV, D, seed=1, device=dev)
+    st = x.state.clone()
+    s1 = pkg.DecodeStep(x.q[0], x.k[0], x.v[0], x.g[0], x.beta[0], st)
+    for _ in range(20):
+        s1()
+    n_sus = 1600
+    a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index or 0) as clk:
+        a_.record()
+        for _ in range(n_sus):
+            s1()
+        b_.record()
+        torch.cuda.synchronize()
+    ms = a_.elapsed_time(b_) / n_sus
+    gbs = inputs.gdn_decode_bytes(B, HQK, HV) / (ms * 1e-3) / 1e9
+    ex[f"sustained_gdn_B{B}"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                                 "steps": n_sus, "seconds": round(ms * n_sus / 1e3, 3),
+                                 "clocks": clk.summary(),
+                                 "note": "the headline kernel timed over >= 1 s back to back "
+                                         "(burst peak as denominator)"}
+    del x, st, s1
     # optional fp16 state (half the streamed state bytes) at the headline size
     x = inputs.make_decode_inputs(1, B, HQK, HV, D, seed=1, device=dev)
     st = x.state.to(torch.float16)
@@ -508,7 +703,8 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
     ex[f"fp16_state_gdn_B{B}"] = {"GBps": round(byts / (ms * 1e-3) / 1e9, 1),
                                   "frac_of_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4),
                                   "tokens_per_s": round(B / (ms * 1e-3), 1), "us": round(ms * 1e3, 2),
-                                  "note": "option, not the BASELINE fp32 state"}
+                                  "note": "option, not the BASELINE fp32 state",
+                                  "cpu_baseline": cpu.get("config1_B256")}
     del x, st, s1
     # config 2: KDA B=64, H=32, 64 steps per replay
     x = inputs.make_decode_inputs(64, 64, 32, 32, D, kda=True, seed=2, device=dev)
@@ -520,53 +716,98 @@ def run_extras(pkg, inputs, dev, hbm, bf16):
     gbs = 64 * inputs.kda_decode_bytes(64, 32, 32) / (ms * 1e-3) / 1e9
     ex["config2_kda_B64_64steps"] = {"GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
                                      "us_per_step": round(ms * 1e3 / 64, 2),
-                                     "note": "268 MB state; partly L2-resident across steps"}
+                                     "note": "268 MB state; partly L2-resident across steps",
+                                     "cpu_baseline": cpu.get("config2")}
     del x, st, s2
     # config 3: chunked prefill
-    try:
-        p = inputs.make_prefill_inputs(4, 4096, HQK, HV, D, seed=3, device=dev)
-        fs = torch.empty((4, HV, D, D), dtype=torch.float32, device=dev)
-        po = torch.empty((4, 4096, HV, D), dtype=torch.bfloat16, device=dev)
-        fn = lambda: pkg.gdn_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
-        for _ in range(3):
-            fn()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        a.record()
-        for _ in range(10):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / 10
-        fl = inputs.gdn_prefill_flops(4, 4096, HQK, HV, D, 64)
-        tf = fl / (ms * 1e-3) / 1e12
-        ex["config3_prefill_B4_T4096"] = {"ms": round(ms, 4), "TFLOPs": round(tf, 1),
-                                          "frac_of_bf16_peak": round(tf / bf16, 4),
-                                          "chunked_form_GFLOP": round(fl / 1e9, 2)}
-    except Exception as e:  # prefill not available yet
-        ex["config3_prefill_B4_T4096"] = {"unavailable": str(e)[:200]}
+    p = inputs.make_prefill_inputs(4, 4096, HQK, HV, D, seed=3, device=dev)
+    fs = torch.empty((4, HV, D, D), dtype=torch.float32, device=dev)
+    po = torch.empty((4, 4096, HV, D), dtype=torch.bfloat16, device=dev)
+    fn = lambda: pkg.gdn_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+    ms = _time_events(fn, reps=10)
+    fl = inputs.gdn_prefill_flops(4, 4096, HQK, HV, D, 64)
+    tf = fl / (ms * 1e-3) / 1e12
+    ex["config3_prefill_B4_T4096"] = {"ms": round(ms, 4), "TFLOPs": round(tf, 1),
+                                      "frac_of_bf16_peak": round(tf / bf16, 4),
+                                      "chunked_form_GFLOP": round(fl / 1e9, 2),
+                                      "cpu_baseline": cpu.get("config3")}
+    del p, fs, po
     # KDA prefill (recurrent form, state on chip) at the config 3 length, H=32
     p = inputs.make_kda_prefill_inputs(4, 4096, 32, 32, D, seed=3, device=dev)
     fs = torch.empty((4, 32, D, D), dtype=torch.float32, device=dev)
     po = torch.empty((4, 4096, 32, D), dtype=torch.bfloat16, device=dev)
     fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
-    for _ in range(2):
+    ms = _time_events(fn, reps=5, warm=2)
+    ex["kda_prefill_B4_T4096_H32"] = {
+        "ms": round(ms, 4), "tokens_per_s": round(4 * 4096 / (ms * 1e-3), 1),
+        "head_tokens_per_s": round(4 * 32 * 4096 / (ms * 1e-3), 1),
+        "fp32_TOPs_recurrent": round(inputs.kda_recurrent_ops(4, 4096, 32, D) / (ms * 1e-3) / 1e12, 2),
+        "GBps_compulsory": round(inputs.kda_prefill_bytes(4, 4096, 32, 32, D) / (ms * 1e-3) / 1e9, 1),
+        "note": "recurrent form on CUDA cores; no tensor cores",
+        "cpu_baseline": cpu.get("kda_prefill")}
+    del p, fs, po
+    return ex
+
+
+def _time_events(fn, reps=10, warm=3):
+    """ms per call of fn(), CUDA events on the current stream after warm-up."""
+    for _ in range(warm):
         fn()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     a.record()
-    for _ in range(5):
+    for _ in range(reps):
         fn()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / 5
-    ex["kda_prefill_B4_T4096_H32"] = {
-        "ms": round(ms, 4), "tokens_per_s": round(4 * 4096 / (ms * 1e-3), 1),
-        "fp32_TOPs_recurrent": round(inputs.kda_recurrent_ops(4, 4096, 32, D) / (ms * 1e-3) / 1e12, 2),
-        "GBps_compulsory": round(inputs.kda_prefill_bytes(4, 4096, 32, 32, D) / (ms * 1e-3) / 1e9, 1),
-        "note": "recurrent form on CUDA cores; no tensor cores"}
-    del p, fs, po
-    return ex
+    return a.elapsed_time(b) / reps
+
+
+def run_seqpar_extras(pkg, inputs, dev, world, rank, bf16):
+    """N > 1: config 3 (B=4, T=4096) split by time over the N ranks with
+    sharded.gdn_prefill_seqpar, timed (CUDA events, max over ranks) and checked
+    on a sampled head against the sequential oracle over the full T."""
+    import numpy as np
+    sharded = graft.submodule("sharded")
+    Bp, Tp = 4, 4096
+    p = inputs.make_prefill_inputs(Bp, Tp, HQK, HV, D, seed=3, device=dev)
+    seg = Tp // world
+    t0 = rank * seg
+    t1 = Tp if rank == world - 1 else t0 + seg
+    x = [t[:, t0:t1].contiguous() for t in (p.q, p.k, p.v, p.g, p.beta)]
+    fn = lambda: sharded.gdn_prefill_seqpar(*x)
+    barrier(world)
+    ms = max_over_ranks(_time_events(fn, reps=5, warm=2), world, dev)
+    single = max_over_ranks(_time_events(lambda: pkg.gdn_prefill(p.q, p.k, p.v, p.g, p.beta), reps=5),
+                            world, dev)
+    fl = inputs.gdn_prefill_flops(Bp, Tp, HQK, HV, D, 64)
+    # parity: sequence b=1, value head 5 (q/k head 2) over the full T
+    bs, hs, hqs = 1, 5, 5 // (HV // HQK)
+    o, S = fn()
+    torch.cuda.synchronize(dev)
+    cpu = [t.float().cpu() for t in (p.q, p.k, p.v, p.g, p.beta)]
+    o_ref, s_ref = graft.oracle().gdn_prefill(cpu[0][bs:bs + 1, :, hqs:hqs + 1],
+                                              cpu[1][bs:bs + 1, :, hqs:hqs + 1],
+                                              cpu[2][bs:bs + 1, :, hs:hs + 1],
+                                              cpu[3][bs:bs + 1, :, hs:hs + 1],
+                                              cpu[4][bs:bs + 1, :, hs:hs + 1])
+    got = o[bs, :, hs].float().cpu().numpy()
+    ref = o_ref[0, t0:t1, 0]
+    err_o = float(np.abs(got - ref).max())
+    bad = float((np.abs(got - ref) - (1e-2 + 2e-2 * np.abs(ref))).max())
+    err_s = float(np.abs(S[bs, hs].cpu().numpy() - s_ref[0, 0]).max()) if rank == world - 1 else 0.0
+    t = torch.tensor([err_o, err_s, bad], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    err_o, err_s, bad = (float(v) for v in t.tolist())
+    tf = fl / (ms * 1e-3) / 1e12
+    return {"seqpar_prefill_B4_T4096": {
+        "ms": round(ms, 4), "TFLOPs_chunked_form": round(tf, 1),
+        "frac_of_bf16_peak_per_job": round(tf / bf16, 4),
+        "single_gpu_prefill_ms": round(single, 4), "speedup_vs_one_gpu": round(single / ms, 3),
+        "segments": f"{world} x T={seg}",
+        "parity": {"checked": True, "sample": "b=1, value head 5, every token; final state on "
+                                              "the last rank", "oracle": "sequential fp32 recurrence",
+                   "max_abs_o": err_o, "max_abs_S": err_s, "ok": bad <= 0.0 and err_s < 1e-3}}}
 
 
 def run_prefill(args, world, rank, local):

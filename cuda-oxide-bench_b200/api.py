@@ -58,6 +58,15 @@ def _require_cuda(*ts: torch.Tensor) -> torch.device:
     return dev
 
 
+def _same_device(ref: torch.Tensor, **named) -> None:
+    """Every named tensor (None = absent) must live on ref's CUDA device: a
+    pointer to host memory or to another GPU would reach the kernel as an
+    address it cannot (or must not) use."""
+    for name, t in named.items():
+        if t is not None and t.device != ref.device:
+            raise GDNError(f"{name} must be on {ref.device}, got {t.device}", 2)
+
+
 def _stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
@@ -88,6 +97,7 @@ def _decode_args(q, k, v, g, beta, state, state_out, o, scale, gate, kda,
                            f"{(B, Hv, dk, dv)} tensor", 2)
     if tuple(o.shape) != (B, Hv, dv) or o.dtype != q.dtype:
         raise GDNError("out must be [B, Hv, d_v] with the dtype of q", 2)
+    _same_device(q, state=state, state_out=state_out, out=o)
     for name, t in (("q", q), ("k", k), ("v", v), ("out", o)):
         if t.stride(-1) != 1:
             raise GDNError(f"{name}: the innermost dimension must be contiguous", 3)
@@ -273,6 +283,7 @@ def _prefill_args(q, k, v, g, beta, initial_state, final_state, o, chunk, scale,
         if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != (B, Hv, dk, dv)
                               or not t.is_contiguous()):
             raise GDNError(f"{name} must be a contiguous fp32 [B, Hv, d_k, d_v] tensor", 2)
+    _same_device(q, initial_state=initial_state, final_state=final_state, out=o)
     a = _lib.PrefillArgs()
     a.q, a.k, a.v, a.g, a.beta = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr()
     a.initial_state = initial_state.data_ptr() if initial_state is not None else None

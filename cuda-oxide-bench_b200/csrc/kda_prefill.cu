@@ -242,10 +242,17 @@ __global__ void __launch_bounds__(kThreads, DK == 256 ? 1 : 2)
         cp_async16(raw + Tr::kRawV + (t * kBV + p * 8) * 2, v + off);
       }
       if (ct < n) {
-        // the aligned 32-bit word holding this token's beta (beta is 4-byte aligned)
-        const uintptr_t e =
-            reinterpret_cast<uintptr_t>(beta + ((tok_base + t0 + ct) * a.Hv + h) * bsz);
-        cp_async4(raw + Tr::kRawBeta + ct * 4, reinterpret_cast<const void*>(e & ~uintptr_t(3)));
+        // the aligned 32-bit word holding this token's beta (beta is 4-byte
+        // aligned).  For a 2-byte beta in the low half of its word, the word
+        // reaches 2 bytes past the element; for the tensor's last element that
+        // is past its end, so that one element is read with a 2-byte load.
+        const int64_t bi = (tok_base + t0 + ct) * a.Hv + h;
+        const uintptr_t e = reinterpret_cast<uintptr_t>(beta + bi * bsz);
+        if (bsz == 2 && (e & 2) == 0 && bi == static_cast<int64_t>(a.B) * a.T * a.Hv - 1)
+          *reinterpret_cast<unsigned short*>(raw + Tr::kRawBeta + ct * 4) =
+              *reinterpret_cast<const unsigned short*>(e);
+        else
+          cp_async4(raw + Tr::kRawBeta + ct * 4, reinterpret_cast<const void*>(e & ~uintptr_t(3)));
       }
       cp_async_commit();
     };

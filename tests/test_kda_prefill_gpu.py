@@ -38,6 +38,22 @@ def test_kda_prefill_matches_oracle(pkg, inputs, orc, B, T, Hqk, Hv, d, init, io
     assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
 
 
+@pytest.mark.parametrize("dk,dv", [(128, 64), (64, 256), (256, 128)])
+def test_kda_prefill_unequal_head_dims(pkg, inputs, orc, dk, dv):
+    """d_k != d_v: the state is [B, Hv, d_k, d_v], the gate [B, T, Hv, d_k]
+    and v / o have d_v columns split into slabs."""
+    B, T, Hqk, Hv = 2, 45, 1, 2
+    p = inputs.make_kda_prefill_inputs(B, T, Hqk, Hv, dk, seed=dk + dv)
+    v = torch.randn((B, T, Hv, dv), generator=torch.Generator().manual_seed(dv)).to(torch.bfloat16)
+    S0 = torch.randn((B, Hv, dk, dv), generator=torch.Generator().manual_seed(3)) * 0.02
+    o_ref, s_ref = orc.kda_prefill(p.q, p.k, v, p.g, p.beta, S0.double().numpy())
+    o, S = pkg.kda_prefill(p.q.to(DEV), p.k.to(DEV), v.to(DEV), p.g.to(DEV), p.beta.to(DEV),
+                           S0.to(DEV), check=True)
+    assert tuple(o.shape) == (B, T, Hv, dv) and tuple(S.shape) == (B, Hv, dk, dv)
+    np.testing.assert_allclose(o.float().cpu().numpy(), o_ref, rtol=O_RTOL, atol=O_ATOL)
+    assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
+
+
 def test_kda_prefill_long_sequence(pkg, inputs, orc):
     """T = 4096 (the prefill length of the GDN prefill config), 8 heads."""
     p = inputs.make_kda_prefill_inputs(1, 4096, 8, 8, 128, seed=4)
