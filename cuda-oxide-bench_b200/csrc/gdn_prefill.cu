@@ -3,7 +3,7 @@
 // The reference defines prefill only as T applications of its decode
 // recurrence (pytorch_reference_gdn.py:38-91; chunking is described, not
 // implemented, in analysis/wave15-attention-research/MECHANISMS.md:398-445).
-// This kernel computes the same result chunk by chunk (chunk C = 64 tokens).
+// This code computes the same result chunk by chunk (chunk C = 64 tokens).
 // Per chunk, with G the in-chunk cumulative log gate, gamma = exp(G):
 //   A[i][j] = beta_i exp(G_i - G_j) k_i.k_j            (j < i)
 //   T       = (I + A)^-1                                (blocked forward substitution, fp32)
@@ -14,28 +14,30 @@
 // which unrolls the recurrence S_t = a_t S_{t-1} + beta_t k_t (v_t - a_t S_{t-1}^T k_t)^T
 // exactly (in exact arithmetic).
 //
+// Two kernels.  Everything that does not depend on the state (the gated
+// K K^T / Q K^T products, the solve, T_w = T diag(beta gamma), T_u = T diag(beta)
+// and the causal decayed P = Q K^T . causal . exp(G_i - G_j)) is independent
+// across chunks, so the first kernel (intra_kernel) computes it for every
+// (batch, q/k head, chunk) at once — 4096 CTAs at config 3, three per SM — and
+// writes bf16 T_w, T_u, P tiles (already in the 128B-swizzled shared-memory
+// layout) plus the fp32 gamma / decay vectors to a workspace.  The second
+// kernel (state_kernel, one CTA per (batch, value head)) runs only the serial
+// state chain over the chunks, fed from the workspace by bulk copies:
+//   helper warps 0-7:  W^T = K^T T_w^T and U^T = V^T T_u^T (tcgen05), the bf16
+//                      W^T tile, outputs of the previous chunk, refills;
+//   state warps 8-15:  V'^T = U^T - S^T W^T (S^T from TMEM, negated A), the
+//                      V'^T / V''^T hi / lo tiles, dS^T = V''^T K (hi + lo),
+//                      Z^T = S^T Q^T, O_intra^T = V'^T P^T, the fp32 state
+//                      update in registers and the bf16 S^T written back to TMEM.
 // Every product is a tcgen05.mma with M = 128, written transposed so the 128
-// TMEM lanes index d_v (or d_k): [K;Q] K^T, W^T = K^T T_w^T, U^T = V^T T_u^T,
-// V'^T = U^T - S^T W^T (accumulated with a negated A onto U), Z^T = S^T Q^T,
-// O_intra^T = V'^T P^T, dS^T = V''^T K.  Operands are bf16 (f16) in
-// 128B-swizzled shared memory (TMA fills K/Q/V; one tile serves as K-major and
-// MN-major operand), except S^T, which lives in TMEM as bf16 and is read as
-// the A operand.  Accumulators use all 512 TMEM columns; the fp32 master state
-// lives in registers of the state warps.
+// TMEM lanes index d_v (or d_k).  Operands are bf16 (f16) in 128B-swizzled
+// shared memory; S^T lives in TMEM as bf16 and is read as the A operand.
 // Precision: the decayed V'' = diag(exp(G_C - G_j)) V' that updates the state
 // is split into bf16 hi + lo halves (two MMAs), and K enters the state update
 // unscaled, so the state accumulates with ~16 mantissa bits per term.
-//
-// One CTA per (batch, value head), 16 warps in two roles that run
-// concurrently, one chunk apart:
-//   intra (warps 0-7):   KQ MMA, A and P rows, T = (I+A)^-1, W/U MMAs, W^T tile
-//                        for chunk c+1 ...
-//   state (warps 8-15):  ... while the state chain of chunk c runs: V' = U - W S,
-//                        V'/V'' tiles, O_intra/dS MMAs, state update, outputs.
-// K/Q/V are double-buffered; the state warps' MMA thread refills a slot with
-// chunk c+2 by TMA as soon as chunk c's last MMA on it has completed.
-// Hand-offs use mbarriers (TMA completion, tcgen05.commit, group arrivals); every
-// wait is bounded and each group agrees on an abort before leaving its loop.
+// Hand-offs use mbarriers (TMA / bulk-copy bytes, tcgen05.commit, group
+// arrivals); every wait is bounded and each group agrees on an abort before
+// leaving its loop.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -49,13 +51,17 @@
 namespace gdn {
 namespace prefill {
 
+constexpr int kC = 64;     // chunk length
+constexpr int kD = 128;    // d_k = d_v
+constexpr int kLd = 68;    // fp32 row stride of the solver matrices
+
 #ifdef GDN_PREFILL_TRACE
-// Phase timestamps of CTA 0 (profiling builds only): [chunk][phase].
+// Phase timestamps of CTA 0 of the state kernel (profiling builds only): [chunk][phase].
 __device__ unsigned long long g_trace[64 * 16];
 #define TRACE(c, ph)                                                                           \
   do {                                                                                         \
-    if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x == 0 || threadIdx.x == kIntraThreads))              \
-      g_trace[(c) * 16 + (ph)] = global_timer_ns();                                            \
+    if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x & 127) == 0 && threadIdx.x < 384)        \
+      g_trace[(c) * 16 + (ph)] = clock64();                                                    \
   } while (0)
 #else
 #define TRACE(c, ph) \
@@ -63,61 +69,21 @@ __device__ unsigned long long g_trace[64 * 16];
   } while (0)
 #endif
 
-constexpr int kC = 64;     // chunk length
-constexpr int kD = 128;    // d_k = d_v
-constexpr int kIntraThreads = 256;
-constexpr int kStateThreads = 256;
-constexpr int kThreads = kIntraThreads + kStateThreads;
-constexpr int kBarIntra = 1, kBarState = 2;  // named barrier ids
-
-// shared-memory map (byte offsets from a 1024-aligned base)
-constexpr uint32_t kKQ = 0;            // 2 slots x [K | Q] tile: 2 d_k blocks x (K 8 KB + Q 8 KB)
-constexpr uint32_t kKQSlot = 32768;
-constexpr uint32_t kKQBlock = 16384;
-constexpr uint32_t kV = 65536;         // 2 slots x V tile: 2 d_v blocks x 8 KB
-constexpr uint32_t kVSlot = 16384;
-constexpr uint32_t kVBlock = 8192;
-constexpr uint32_t kTw = 98304;        // T diag(beta gamma), K-major rows i   (8 KB)
-constexpr uint32_t kTu = 106496;       // T diag(beta), K-major rows i          (8 KB)
-constexpr uint32_t kP = 114688;        // 2 slots x causal decayed QK^T        (8 KB each)
-constexpr uint32_t kPSlot = 8192;
-constexpr uint32_t kWT = 131072;       // W^T, MN-major rows d_k               (16 KB)
-constexpr uint32_t kVP = 147456;       // V'^T, K-major rows d_v               (16 KB)
-constexpr uint32_t kVH = 163840;       // V''^T hi                             (16 KB)
-constexpr uint32_t kVL = 180224;       // V''^T lo                             (16 KB)
-constexpr int kLd = 68;                // fp32 row stride of the solver matrices
-constexpr uint32_t kAT = 196608;       // A, overwritten in place by T: [64][68] fp32
-constexpr uint32_t kMs = kTw;          // solver scratch [32][68] fp32 (aliases T_w/T_u,
-                                       // which are written only after the solve)
-constexpr uint32_t kVec = kAT + 64 * kLd * 4;  // 3 slots x {G, gamma, beta, decay} x 64 fp32
-constexpr int kVecSlot = 4 * 64;               // floats per slot
-constexpr uint32_t kBars = kVec + 3 * kVecSlot * 4;
-constexpr uint32_t kSmemBytes = kBars + 256;
-constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // + alignment slack
-static_assert(32 * kLd * 4 <= 2 * 8192, "solver scratch overflows its alias");
-
-// TMEM columns
-constexpr uint32_t kTmST = 0;    // S^T bf16, packed pairs: 64 columns
-constexpr uint32_t kTmKQ = 64;   // [K;Q]K^T, then reused for W^T
-constexpr uint32_t kTmU = 128;   // 2 slots x U^T / V'^T
-constexpr uint32_t kTmZ = 256, kTmOI = 320, kTmDS = 384, kTmCols = 512;
-
-// mbarrier indices
-enum {
-  kBarKQV = 0,        // [2] TMA of a K/Q/V slot landed
-  kBarIMma = 2,       // intra MMA completion
-  kBarReady = 3,      // [2] intra -> state: W^T tile, U, P, gates of a chunk ready
-  kBarX = 5,          // V' = U - W S done (W^T tile free)
-  kBarZ = 6,          // Z done
-  kBarS2 = 7,         // O_intra and dS done
-  kBarSlotFree = 8,   // [2] a K/Q/V, U and P slot may be refilled
-  kNumBars = 10,
-};
+// Workspace record of one (batch, value head, chunk): bf16 tiles in the
+// 128B-swizzled layout of a 64 x 64 K-major operand (rows i, 1024-byte
+// atoms), then the fp32 vectors.
+constexpr uint32_t kWsTw = 0;        // T diag(beta gamma)   rows i, cols j
+constexpr uint32_t kWsTu = 8192;     // T diag(beta)
+constexpr uint32_t kWsP = 16384;     // Q K^T . causal . exp(G_i - G_j)
+constexpr uint32_t kWsVec = 24576;   // gamma[64], exp(G_C - G_j)[64] fp32
+constexpr uint32_t kWsUnit = 25088;
+static_assert(kWsUnit % 16 == 0 && kWsP % 16 == 0 && kWsVec % 16 == 0, "bulk-copy alignment");
 
 struct Params {
   gdn_prefill_args_t a;
   int32_t nchunks;
   int32_t group;
+  unsigned char* ws;
 };
 
 template <bool BF16>
@@ -127,6 +93,19 @@ __device__ __forceinline__ void store_row16(uint32_t tile, int row, int chunk0, 
   tc::sts128(tile + tc::sw128_offset(row, chunk0 + 1), tc::pack2<BF16>(v[8], v[9]),
              tc::pack2<BF16>(v[10], v[11]), tc::pack2<BF16>(v[12], v[13]),
              tc::pack2<BF16>(v[14], v[15]));
+}
+
+// Same layout, written to a global-memory copy of the tile.
+template <bool BF16>
+__device__ __forceinline__ void store_row16_global(unsigned char* tile, int row, int chunk0,
+                                                   const float* v) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float* w = v + 8 * h;
+    uint4 u = make_uint4(tc::pack2<BF16>(w[0], w[1]), tc::pack2<BF16>(w[2], w[3]),
+                         tc::pack2<BF16>(w[4], w[5]), tc::pack2<BF16>(w[6], w[7]));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(row, chunk0 + h)) = u;
+  }
 }
 
 // Bounded wait polled by lane 0 of each warp (the other lanes sleep in the
@@ -183,15 +162,16 @@ __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], 
 }
 
 // In place: AT holds strictly-lower A (64 x 64 fp32, stride kLd, zeros on and
-// above the diagonal) and is overwritten with T = (I + A)^-1.  Run by the
-// intra warps (warps 0-3 compute; the others only join the group barriers).  Steps: the four 16 x 16 diagonal blocks D_r by
-// forward substitution (one warp each, one lane per column, fp32); T_10 =
-// -D_1 A_10 D_0 and T_32 = -D_3 A_32 D_2; then the lower-left quadrant
-// -T_bot A_bl T_top through Y = A_bl T_top (TF32 warp MMAs).  Each block of A is last read
-// before the block of T that replaces it is written.
-__device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, int lane) {
-  if (warp < 4) {
-    const int bb = warp * 16, c = lane & 15;
+// above the diagonal) and is overwritten with T = (I + A)^-1.  Run by one
+// group of four warps (w = 0..3 inside the group) that syncs on named barrier
+// `bar` (128 threads).  Steps: the four 16 x 16 diagonal blocks D_r by forward
+// substitution (one warp each, one lane per column, fp32); T_10 = -D_1 A_10 D_0
+// and T_32 = -D_3 A_32 D_2; then the lower-left quadrant -T_bot A_bl T_top
+// through Y = A_bl T_top (TF32 warp MMAs).  Each block of A is last read
+// before the block of T that replaces it is written.  M is [32][kLd] scratch.
+__device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int lane, int bar) {
+  {
+    const int bb = w * 16, c = lane & 15;
     float t[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) t[i] = (i == c) ? 1.f : 0.f;
@@ -215,10 +195,10 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
       for (int i = 0; i < 16; ++i) AT[(bb + i) * kLd + bb + c] = t[i];
     }
   }
-  tc::group_sync(kBarIntra, kIntraThreads);
-  if (warp < 2) {  // T_10 (warp 0) and T_32 (warp 1)
-    const int c = warp * 2, r = c + 1;
-    float* X = M + warp * 16 * kLd;
+  tc::group_sync(bar, 128);
+  if (w < 2) {  // T_10 (w 0) and T_32 (w 1)
+    const int c = w * 2, r = c + 1;
+    float* X = M + w * 16 * kLd;
     float acc[2][4] = {};
     block_mma(acc, AT + 16 * r * kLd + 16 * c, AT + 16 * c * kLd + 16 * c, lane);
     block_store(X, acc, 1.f, lane);
@@ -227,9 +207,9 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
     block_mma(acc2, AT + 16 * r * kLd + 16 * r, X, lane);
     block_store(AT + 16 * r * kLd + 16 * c, acc2, -1.f, lane);
   }
-  tc::group_sync(kBarIntra, kIntraThreads);
-  if (warp < 4) {  // Y_rc = sum_k A_rk T_kc over the top blocks, warp (r-2)*2 + c
-    const int r = 2 + (warp >> 1), c = warp & 1;
+  tc::group_sync(bar, 128);
+  {  // Y_rc = sum_k A_rk T_kc over the top blocks, warp (r-2)*2 + c
+    const int r = 2 + (w >> 1), c = w & 1;
     float acc[2][4] = {};
     if (c == 0) {
       block_mma(acc, AT + 16 * r * kLd + 0, AT + 0, lane);                      // A_r0 D_0
@@ -239,9 +219,9 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
     }
     block_store(M + (r - 2) * 16 * kLd + 16 * c, acc, 1.f, lane);
   }
-  tc::group_sync(kBarIntra, kIntraThreads);
-  if (warp < 4) {
-    const int r = 2 + (warp >> 1), c = warp & 1;
+  tc::group_sync(bar, 128);
+  {
+    const int r = 2 + (w >> 1), c = w & 1;
     float acc[2][4] = {};
     if (r == 2) {
       block_mma(acc, AT + 32 * kLd + 32, M + 16 * c, lane);                     // D_2 Y_2c
@@ -251,8 +231,290 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int warp, 
     }
     block_store(AT + 16 * r * kLd + 16 * c, acc, -1.f, lane);
   }
-  tc::group_sync(kBarIntra, kIntraThreads);
+  tc::group_sync(bar, 128);
 }
+
+// ============================================================ intra kernel
+// One CTA per (batch, q/k head, chunk), 8 warps; warps 4h..4h+3 serve value
+// head (pair index) h of the q/k head's group, so a GQA pair shares the
+// K K^T / Q K^T product.  Chunks run last-to-first so that the state kernel,
+// which starts at chunk 0, finds the most recent records still in L2.
+namespace intra {
+constexpr int kThreads = 256;
+constexpr uint32_t kKQ = 0;                      // [K | Q] per d_k block: 2 x 16 KB
+constexpr uint32_t kKQBlock = 16384;
+constexpr uint32_t kATHead = 64 * kLd * 4;       // 17408
+constexpr uint32_t kAT = 32768;                  // [2 heads] A -> T in place
+constexpr uint32_t kMsHead = 32 * kLd * 4;       // 8704: solver scratch per head, aliasing
+                                                 // the K/Q tiles once the MMA is done
+constexpr uint32_t kVec = kAT + 2 * kATHead;     // [2 heads][G|beta|gamma|decay|Ee|Es][64]
+constexpr uint32_t kFlags = kVec + 2 * 6 * 64 * 4;
+constexpr uint32_t kBars = kFlags + 16;
+constexpr uint32_t kSmemBytes = kBars + 64;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
+static_assert(2 * kMsHead <= kAT, "solver scratch overflows the K/Q tiles");
+}  // namespace intra
+
+template <bool BF16>
+__global__ void __launch_bounds__(intra::kThreads, 3)
+    intra_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
+                 const __grid_constant__ CUtensorMap map_k) {
+  using namespace intra;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);  // [0] TMA, [1] MMA
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2);
+
+  const gdn_prefill_args_t& a = p.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hh = warp >> 2, w4 = warp & 3, ht = tid & 127;
+  const int per_c = a.B * a.Hqk;
+  const int c = p.nchunks - 1 - static_cast<int>(blockIdx.x) / per_c;
+  const int bq = static_cast<int>(blockIdx.x) % per_c;
+  const int b = bq / a.Hqk, hq = bq % a.Hqk;
+  const int T = a.T, t0 = c * kC;
+
+  if (warp == 0) tc::tmem_alloc(tmem_holder, 64);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t lane_base = static_cast<uint32_t>(w4 * 32) << 16;
+  constexpr uint32_t kIdKQ = tc::idesc_f16(128, 64, false, false, BF16);
+
+  bool ok = true;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], 4 * 8192);
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      unsigned char* kq = smem + kKQ + blk * kKQBlock;
+      tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
+      tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
+    }
+    // [K;Q] K^T: TMEM lanes 0-63 hold K K^T rows, lanes 64-127 Q K^T rows
+    ok = mbar_wait_bounded(&bars[0], 0);
+    if (ok) {
+      tc::fence_after_sync();
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        tc::mma(tmem, tc::kmajor_desc(sb + kKQ, kKQBlock, s), tc::kmajor_desc(sb + kKQ, kKQBlock, s),
+                kIdKQ, s > 0);
+      tc::commit(&bars[1]);
+    }
+  }
+  // Every warp learns whether the product is coming; lane 0 of each warp then
+  // waits for it (bounded) and the CTA votes.
+  ok = !named_barrier_or(1, kThreads, !ok);
+  if (ok) {
+    bool mine = true;
+    if (lane == 0) mine = mbar_wait_bounded(&bars[1], 0);
+    ok = !named_barrier_or(1, kThreads, !mine);
+  }
+  if (!ok) {
+    if (tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
+  } else {
+    tc::fence_after_sync();
+    const int bar = 2 + hh;
+    float* AT = reinterpret_cast<float*>(smem + kAT + hh * kATHead);
+    float* Ms = reinterpret_cast<float*>(smem + kKQ + hh * kMsHead);
+    float* sG = reinterpret_cast<float*>(smem + kVec) + hh * 384;
+    float* sBeta = sG + 64;
+    float* sGam = sG + 128;
+    float* sDec = sG + 192;
+    float* sEe = sG + 256;   // exp(G_end(J) - G_j)
+    float* sEs = sG + 320;   // exp(G_start(J) - G_j)
+    int* sFast = reinterpret_cast<int*>(smem + kFlags) + hh;
+    for (int p0 = 0; p0 < p.group; p0 += 2) {
+      const bool active = p0 + hh < p.group;  // an odd group leaves warps 4-7 idle
+      const int h = hq * p.group + p0 + hh;
+      unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
+      if (active && ht < kC) {
+        const int t = t0 + ht;
+        float gv = 0.f, bv = 0.f;  // padded tokens: no decay, no update
+        if (t < T) {
+          const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + h;
+          gv = load_any(a.g, gi, a.g_dtype);
+          bv = load_any(a.beta, gi, a.beta_dtype);
+        }
+        sG[ht] = gv;
+        sBeta[ht] = bv;
+      }
+      tc::group_sync(bar, 128);
+      if (active && w4 == 0) {  // in-chunk cumulative log gate; lane l owns tokens 2l, 2l+1
+        const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
+        float run = g0 + g1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float o = __shfl_up_sync(0xffffffffu, run, off);
+          if (lane >= off) run += o;
+        }
+        const float excl = run - (g0 + g1);
+        const float GC = __shfl_sync(0xffffffffu, run, 31);
+        const float Ga = excl + g0, Gb = run;
+        // G at the first and last token of this lane's 16-token block
+        const float Gs = __shfl_sync(0xffffffffu, Ga, lane & ~7);
+        const float Ge = __shfl_sync(0xffffffffu, Gb, lane | 7);
+        // the factored exponentials below stay finite when no block decays by
+        // more than 80 (nats) within itself; otherwise the direct form is used
+        const bool fast = __all_sync(0xffffffffu, Gs - Ge <= 80.f);
+        __syncwarp();
+        sG[2 * lane] = Ga;
+        sG[2 * lane + 1] = Gb;
+        const float2 gam = make_float2(__expf(Ga), __expf(Gb));
+        const float2 dec = make_float2(__expf(GC - Ga), __expf(GC - Gb));  // V'' row scale
+        reinterpret_cast<float2*>(sGam)[lane] = gam;
+        reinterpret_cast<float2*>(sDec)[lane] = dec;
+        reinterpret_cast<float2*>(sEe)[lane] = make_float2(__expf(Ge - Ga), __expf(Ge - Gb));
+        reinterpret_cast<float2*>(sEs)[lane] =
+            make_float2(__expf(fminf(Gs - Ga, 80.f)), __expf(fminf(Gs - Gb, 80.f)));
+        if (lane == 0) *sFast = fast ? 1 : 0;
+        reinterpret_cast<float2*>(rec + kWsVec)[lane] = gam;
+        reinterpret_cast<float2*>(rec + kWsVec + 256)[lane] = dec;
+      }
+      tc::group_sync(bar, 128);
+      if (active) {  // A rows (TMEM lanes 0-63, warps 0-1) and P rows (lanes 64-127, warps 2-3)
+        // exp(G_i - G_j) for j <= i, factored by 16-token blocks I = i/16, J = j/16:
+        //   J < I : exp(G_i - G_end(J)) exp(G_end(J) - G_j)     (both factors <= 1)
+        //   J = I : exp(G_i - G_start(I)) exp(G_start(I) - G_j) (fast path) or direct
+        // so each row needs four exponentials instead of one per element.
+        const int i = (w4 & 1) * 32 + lane;
+        const int I = i >> 4;
+        const float Gi = sG[i];
+        const float bi = sBeta[i];
+        const bool fast = *sFast != 0;
+        float rf[3];
+#pragma unroll
+        for (int J = 0; J < 3; ++J) rf[J] = (J < I) ? __expf(Gi - sG[16 * J + 15]) : 0.f;
+        const float rd = __expf(Gi - sG[16 * I]);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          float r[32];
+          if ((w4 & 1) == 0 && cb == 1) {  // rows 0-31, columns 32-63: above the diagonal
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) r[jj] = 0.f;
+          } else {
+            tc::tmem_ld16(tmem + lane_base + cb * 32, *reinterpret_cast<float(*)[16]>(r));
+            tc::tmem_ld16(tmem + lane_base + cb * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+            tc::tmem_wait_ld();
+            const float row_s = w4 < 2 ? bi : 1.f;
+            const int lim = w4 < 2 ? i : i + 1;  // A: j < i; P: j <= i
+            if (fast) {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                const int j = cb * 32 + jj, J = j >> 4;
+                const float e = (J < I) ? rf[J < 3 ? J : 2] * sEe[j] : rd * sEs[j];
+                r[jj] = (j < lim) ? row_s * e * r[jj] : 0.f;
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                const int j = cb * 32 + jj;
+                r[jj] = (j < lim) ? row_s * __expf(Gi - sG[j]) * r[jj] : 0.f;
+              }
+            }
+          }
+          if (w4 < 2) {
+#pragma unroll
+            for (int j4 = 0; j4 < 32; j4 += 4)
+              *reinterpret_cast<float4*>(AT + i * kLd + cb * 32 + j4) =
+                  make_float4(r[j4], r[j4 + 1], r[j4 + 2], r[j4 + 3]);
+          } else {
+            store_row16_global<BF16>(rec + kWsP, i, cb * 4, r);
+            store_row16_global<BF16>(rec + kWsP, i, cb * 4 + 2, r + 16);
+          }
+        }
+      }
+      tc::group_sync(bar, 128);
+      if (active) solve_unit_lower(AT, Ms, w4, lane, bar);
+      if (active) {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 32 columns
+        const int i = ht >> 1, jh = ht & 1;
+        float tw[32], tu[32];
+#pragma unroll
+        for (int j4 = 0; j4 < 32; j4 += 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jh * 32 + j4);
+          const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = jh * 32 + j4 + e;
+            const float t = (j <= i) ? tv[e] : 0.f;
+            tu[j4 + e] = t * sBeta[j];
+            tw[j4 + e] = tu[j4 + e] * sGam[j];
+          }
+        }
+        store_row16_global<BF16>(rec + kWsTw, i, jh * 4, tw);
+        store_row16_global<BF16>(rec + kWsTw, i, jh * 4 + 2, tw + 16);
+        store_row16_global<BF16>(rec + kWsTu, i, jh * 4, tu);
+        store_row16_global<BF16>(rec + kWsTu, i, jh * 4 + 2, tu + 16);
+      }
+      tc::group_sync(bar, 128);  // AT and the vectors are reused by the next pair
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 64);
+}
+
+// ============================================================ state kernel
+// One CTA per (batch, value head), 16 warps in three roles:
+//   W group  (warps 0-3):  W^T = K^T T_w^T, U^T = V^T T_u^T, the bf16 W^T tile,
+//                          refills of V / T_w / T_u;
+//   O group  (warps 4-7):  Q rows scaled by gamma_i in place (so that
+//                          diag(gamma) Q S and the intra-chunk term accumulate
+//                          into one TMEM accumulator), outputs, K/Q/P refills;
+//   state    (warps 8-15): the serial chain X -> V' -> dS -> S.
+namespace state {
+constexpr int kGroupThreads = 128;  // W group, O group
+constexpr int kStateThreads = 256;
+constexpr int kThreads = 2 * kGroupThreads + kStateThreads;
+constexpr int kBarW = 1, kBarState = 2, kBarO = 3;  // named barrier ids
+
+// shared-memory map (byte offsets from a 1024-aligned base)
+constexpr uint32_t kKQ = 0;          // 3 slots x [K | Q]: 2 d_k blocks x (K 8 KB + Q 8 KB)
+constexpr uint32_t kKQSlot = 32768;
+constexpr uint32_t kKQBlock = 16384;
+constexpr uint32_t kP = 98304;       // 3 slots x {P tile (8 KB), gamma[64], decay[64]}
+constexpr uint32_t kPSlot = 9216;
+constexpr uint32_t kV = 126976;      // V tile: 2 d_v blocks x 8 KB (one slot)
+constexpr uint32_t kVBlock = 8192;
+constexpr uint32_t kTw = 143360;     // T_w tile (8 KB), then T_u (8 KB): one slot
+constexpr uint32_t kTu = 151552;
+constexpr uint32_t kWT = 159744;     // W^T, MN-major rows d_k               (16 KB)
+constexpr uint32_t kVP = 176128;     // V'^T, K-major rows d_v               (16 KB)
+constexpr uint32_t kOut = 192512;    // output staging [64][128] io          (16 KB)
+constexpr uint32_t kBars = 208896;
+constexpr uint32_t kSmemBytes = kBars + 256;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
+static_assert(kP % 1024 == 0 && kPSlot % 1024 == 0 && kV % 1024 == 0 && kTw % 1024 == 0 &&
+              kWT % 1024 == 0 && kVP % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+// TMEM columns
+constexpr uint32_t kTmST = 0;    // S^T bf16, packed pairs: 64 columns
+constexpr uint32_t kTmW = 64;    // W^T
+constexpr uint32_t kTmU = 128;   // 2 slots x U^T / V'^T, then V''^T hi | lo (bf16 pairs)
+constexpr uint32_t kTmO = 256;   // 2 slots x O^T = S^T (diag(gamma) Q)^T + V'^T P^T
+constexpr uint32_t kTmDS = 384, kTmCols = 512;
+
+// mbarrier indices
+enum {
+  kBarKQP = 0,     // [3] K, Q (TMA), P and the vectors (bulk) of a chunk landed
+  kBarTWU = 3,     // V (TMA), T_w | T_u (bulk) of a chunk landed
+  kBarHMma = 4,    // W/U MMAs completed
+  kBarReady = 5,   // [2] W group -> state: W^T tile and U of a chunk ready
+  kBarQ = 7,       // [3] O group -> state: Q of a chunk scaled by gamma (by K/Q/P slot)
+  kBarOFree = 10,  // [2] O group finished reading an O slot
+  kBarX = 12,      // V' = U - W S done
+  kBarS2 = 13,     // dS done
+  kBarZO = 14,     // [2] O of a chunk complete (its K/Q/P slot is free)
+  kNumBars = 16,
+};
+}  // namespace state
 
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
@@ -260,21 +522,18 @@ __device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
-                   const __grid_constant__ CUtensorMap map_k,
-                   const __grid_constant__ CUtensorMap map_v) {
+__global__ void __launch_bounds__(state::kThreads, 1)
+    state_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
+                 const __grid_constant__ CUtensorMap map_k,
+                 const __grid_constant__ CUtensorMap map_v) {
+  using namespace state;
   using IO = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
-  float* vec = reinterpret_cast<float*>(smem + kVec);  // [slot][G | gamma | beta][64]
-  float* AT = reinterpret_cast<float*>(smem + kAT);
-  float* Ms = reinterpret_cast<float*>(smem + kMs);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars + 1);
 
   const gdn_prefill_args_t& a = p.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -282,20 +541,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bh / a.Hv, h = bh % a.Hv, hq = h / p.group;
   const int T = a.T;
   const int nchunks = p.nchunks;
+  const unsigned char* recs = p.ws + static_cast<size_t>(bh) * nchunks * kWsUnit;
+  auto pvec = [&](int c) {  // {gamma[64], decay[64]} of chunk c (in its K/Q/P slot)
+    return reinterpret_cast<const float*>(smem + kP + (c % 3) * kPSlot + 8192);
+  };
 
   if (warp == 0) tc::tmem_alloc(tmem_holder, kTmCols);
   if (tid == 0) {
-    mbar_init(&bars[kBarKQV], 1);
-    mbar_init(&bars[kBarKQV + 1], 1);
-    mbar_init(&bars[kBarIMma], 1);
-    mbar_init(&bars[kBarReady], kIntraThreads);
-    mbar_init(&bars[kBarReady + 1], kIntraThreads);
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[kBarKQP + i], 1);
+    mbar_init(&bars[kBarTWU], 1);
+    mbar_init(&bars[kBarHMma], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[kBarReady + i], kGroupThreads);
+      mbar_init(&bars[kBarOFree + i], kGroupThreads);
+    }
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[kBarQ + i], kGroupThreads);
     mbar_init(&bars[kBarX], 1);
-    mbar_init(&bars[kBarZ], 1);
     mbar_init(&bars[kBarS2], 1);
-    mbar_init(&bars[kBarSlotFree], 1);
-    mbar_init(&bars[kBarSlotFree + 1], 1);
-    *abort_flag = 0;
+    mbar_init(&bars[kBarZO], 1);
+    mbar_init(&bars[kBarZO + 1], 1);
     fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -308,180 +572,69 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kIdXneg = tc::idesc_f16(128, 64, false, true, BF16, true);
   constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, BF16);
 
-  auto issue_tma = [&](int n) {  // K, Q, V of chunk n into slot n & 1
-    const int slot = n & 1;
-    uint64_t* bar = &bars[kBarKQV + slot];
-    mbar_arrive_expect_tx(bar, 6 * 8192);
+  auto issue_kqp = [&](int n) {  // K, Q (TMA), P and vectors (bulk) of chunk n into slot n % 3
+    const int slot = n % 3;
+    uint64_t* bar = &bars[kBarKQP + slot];
+    mbar_arrive_expect_tx(bar, 4 * 8192 + 8192 + 512);
     const int t0 = n * kC;
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
       unsigned char* kq = smem + kKQ + slot * kKQSlot + blk * kKQBlock;
       tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, bar);
       tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, bar);
-      tc::tma_load_4d(smem + kV + slot * kVSlot + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
     }
+    const unsigned char* rec = recs + static_cast<size_t>(n) * kWsUnit;
+    bulk_g2s(smem + kP + slot * kPSlot, rec + kWsP, 8192, bar);
+    bulk_g2s(smem + kP + slot * kPSlot + 8192, rec + kWsVec, 512, bar);
   };
-  if (tid == kIntraThreads) {
-    issue_tma(0);
-    if (nchunks > 1) issue_tma(1);
+  auto issue_twu = [&](int n) {  // V (TMA), T_w | T_u (bulk) of chunk n
+    uint64_t* bar = &bars[kBarTWU];
+    mbar_arrive_expect_tx(bar, 2 * 8192 + 16384);
+    const int t0 = n * kC;
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk)
+      tc::tma_load_4d(smem + kV + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
+    bulk_g2s(smem + kTw, recs + static_cast<size_t>(n) * kWsUnit + kWsTw, 16384, bar);
+  };
+  if (tid == 2 * kGroupThreads) {
+    for (int n = 0; n < 3 && n < nchunks; ++n) issue_kqp(n);
+    issue_twu(0);
   }
 
-  if (warp < kIntraThreads / 32) {
-    // ================================================================ intra
+  if (warp < 4) {
+    // ================================================================ W group
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
-    const int it = tid;  // 0..255
-    const int quarter = warp & 3, ih = warp >> 2;
-    float g_next = 0.f, b_next = 0.f;
-    auto load_gates = [&](int chunk) {
-      const int t = chunk * kC + it;
-      g_next = 0.f;
-      b_next = 0.f;
-      if (it < kC && t < T) {
-        const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + h;
-        g_next = load_any(a.g, gi, a.g_dtype);
-        b_next = load_any(a.beta, gi, a.beta_dtype);
-      }
-    };
-    load_gates(0);
-    uint32_t imma_phase = 0;
+    const int k = warp * 32 + lane;  // W^T row (d_k) this thread converts
+    bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c & 1;
-      float* sG = vec + (c % 3) * kVecSlot;
-      float* sGam = sG + 64;
-      float* sBeta = sG + 128;
-      float* sDecay = sG + 192;
-      const uint32_t kq = sb + kKQ + slot * kKQSlot;
-      const uint32_t vt = sb + kV + slot * kVSlot;
-      const uint32_t pt = sb + kP + slot * kPSlot;
+      const uint32_t kq = sb + kKQ + (c % 3) * kKQSlot;
       const uint32_t tmu = tmem + kTmU + slot * 64;
-      float graw = g_next;
-      if (it < kC) sBeta[it] = b_next;
-      if (!group_wait(&bars[kBarKQV + slot], (c >> 1) & 1, kBarIntra, kIntraThreads)) break;
+      if (!group_wait(&bars[kBarKQP + c % 3], (c / 3) & 1, kBarW, kGroupThreads)) { ok = false; break; }
+      if (!group_wait(&bars[kBarTWU], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
+      // the U slot was last used by chunk c - 2 (its dS MMA precedes X of c - 1)
+      // and the W^T tile by X of chunk c - 1
+      if (c >= 1 && !group_wait(&bars[kBarX], (c - 1) & 1, kBarW, kGroupThreads)) { ok = false; break; }
       TRACE(c, 0);
-      if (it == 0) {
+      if (tid == 0) {  // W^T = K^T T_w^T, U^T = V^T T_u^T
         tc::fence_after_sync();
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          tc::mma(tmem + kTmKQ, tc::kmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(kq, kKQBlock, s),
-                  kIdKQ, s > 0);
-        tc::commit(&bars[kBarIMma]);
-      }
-      if (c + 1 < nchunks) load_gates(c + 1);
-      // in-chunk cumulative log gate: threads 0..63 publish the raw gates, then
-      // warp 0 scans them (lane l owns tokens 2l, 2l+1)
-      if (it < kC) sG[it] = graw;
-      tc::group_sync(kBarIntra, kIntraThreads);
-      if (warp == 0) {
-        const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
-        float run = g0 + g1;
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmem + kTmW, tc::mnmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(sb + kTw, 0, s), kIdW, s > 0);
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float o = __shfl_up_sync(0xffffffffu, run, off);
-          if (lane >= off) run += o;
-        }
-        const float excl = run - (g0 + g1);
-        const float GC = __shfl_sync(0xffffffffu, run, 31);
-        __syncwarp();
-        sG[2 * lane] = excl + g0;
-        sG[2 * lane + 1] = run;
-        sGam[2 * lane] = __expf(excl + g0);
-        sGam[2 * lane + 1] = __expf(run);
-        sDecay[2 * lane] = __expf(GC - (excl + g0));  // exp(G_C - G_j): V'' row scale
-        sDecay[2 * lane + 1] = __expf(GC - run);
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmu, tc::mnmajor_desc(sb + kV, kVBlock, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+        tc::commit(&bars[kBarHMma]);
       }
-      // P and U of this slot were last used by chunk c-2: wait until it is done
-      if (c >= 2 && !group_wait(&bars[kBarSlotFree + slot], ((c - 2) >> 1) & 1, kBarIntra, kIntraThreads))
-        break;
-      if (!group_wait(&bars[kBarIMma], imma_phase, kBarIntra, kIntraThreads)) break;
-      imma_phase ^= 1;
+      if (!group_wait(&bars[kBarHMma], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
       tc::fence_after_sync();
+      if (tid == 0 && c + 1 < nchunks) issue_twu(c + 1);  // V / T_w / T_u slot is free again
       TRACE(c, 1);
-      {  // A rows (TMEM lanes 0-63) and P rows (lanes 64-127); warps w and w+4
-         // take columns [0, 32) and [32, 64)
-        const int i = (quarter & 1) * 32 + lane;
+#pragma unroll
+      for (int ih = 0; ih < 2; ++ih) {  // W^T -> bf16 tile, MN-major rows d_k, tokens [32 ih, +32)
         float r[32];
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb)
-          tc::tmem_ld16(tmem + lane_base + kTmKQ + ih * 32 + cb * 16,
-                        *reinterpret_cast<float(*)[16]>(r + cb * 16));
-        tc::tmem_wait_ld();
-        TRACE(c, 12);
-        const float Gi = sG[i];
-        if (quarter < 2) {
-          const float bi = sBeta[i];
-#pragma unroll
-          for (int j4 = 0; j4 < 32; j4 += 4) {
-            float4 v;
-            float* pv = reinterpret_cast<float*>(&v);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = ih * 32 + j4 + e;
-              pv[e] = (j < i) ? bi * __expf(Gi - sG[j]) * r[j4 + e] : 0.f;
-            }
-            *reinterpret_cast<float4*>(AT + i * kLd + ih * 32 + j4) = v;
-          }
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = ih * 32 + jj;
-            r[jj] = (j <= i) ? r[jj] * __expf(Gi - sG[j]) : 0.f;
-          }
-          store_row16<BF16>(pt, i, ih * 4, r);
-          store_row16<BF16>(pt, i, ih * 4 + 2, r + 16);
-        }
-      }
-      TRACE(c, 13);
-      tc::fence_before_sync();
-      tc::group_sync(kBarIntra, kIntraThreads);
-      TRACE(c, 2);
-      solve_unit_lower(AT, Ms, warp, lane);
-      TRACE(c, 3);
-      {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 16 columns
-        const int i = it >> 2, jq = it & 3;
-        float tw[16], tu[16];
-#pragma unroll
-        for (int j4 = 0; j4 < 16; j4 += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jq * 16 + j4);
-          const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = jq * 16 + j4 + e;
-            const float t = (j <= i) ? tv[e] : 0.f;
-            tu[j4 + e] = t * sBeta[j];
-            tw[j4 + e] = tu[j4 + e] * sGam[j];
-          }
-        }
-        store_row16<BF16>(sb + kTw, i, jq * 2, tw);
-        store_row16<BF16>(sb + kTu, i, jq * 2, tu);
-      }
-      tc::fence_proxy_async();
-      tc::fence_before_sync();
-      tc::group_sync(kBarIntra, kIntraThreads);
-      TRACE(c, 4);
-      if (it == 0) {  // W^T = K^T T_w^T (reuses the KQ columns), U^T = V^T T_u^T
-        tc::fence_after_sync();
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma(tmem + kTmKQ, tc::mnmajor_desc(kq, kKQBlock, s), tc::kmajor_desc(sb + kTw, 0, s),
-                  kIdW, s > 0);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma(tmu, tc::mnmajor_desc(vt, kVBlock, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
-        tc::commit(&bars[kBarIMma]);
-      }
-      // the W^T tile was read by the previous chunk's V' MMA: wait for it
-      if (c >= 1 && !group_wait(&bars[kBarX], (c - 1) & 1, kBarIntra, kIntraThreads)) break;
-      if (!group_wait(&bars[kBarIMma], imma_phase, kBarIntra, kIntraThreads)) break;
-      imma_phase ^= 1;
-      tc::fence_after_sync();
-      TRACE(c, 5);
-      {  // W^T -> bf16 tile, MN-major rows d_k = quarter*32 + lane, tokens [32 ih, +32)
-        const int k = quarter * 32 + lane;
-        float r[32];
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb)
-          tc::tmem_ld16(tmem + lane_base + kTmKQ + ih * 32 + cb * 16,
-                        *reinterpret_cast<float(*)[16]>(r + cb * 16));
+        tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32, *reinterpret_cast<float(*)[16]>(r));
+        tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
         tc::tmem_wait_ld();
         store_row16<BF16>(sb + kWT, k, ih * 4, r);
         store_row16<BF16>(sb + kWT, k, ih * 4 + 2, r + 16);
@@ -489,17 +642,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async();
       tc::fence_before_sync();
       mbar_arrive(&bars[kBarReady + slot]);
-      TRACE(c, 6);
+      TRACE(c, 2);
     }
+    if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
+  } else if (warp < 8) {
+    // ================================================================ O group
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    const int ot = tid - kGroupThreads;  // 0..127
+    const int dv = (warp & 3) * 32 + lane;
+    IO* o = static_cast<IO*>(a.o);
+    // outputs o[t0 + i][dv] = scale O[dv][i]: staged as a [64][128] tile, then
+    // written with coalesced 16-byte stores; the slot of chunk c is then
+    // refilled with chunk c + 3
+    auto outputs = [&](int c) -> bool {
+      if (!group_wait(&bars[kBarZO + (c & 1)], (c >> 1) & 1, kBarO, kGroupThreads)) return false;
+      tc::fence_after_sync();
+      IO* stage = reinterpret_cast<IO*>(smem + kOut);
+      const uint32_t tmo = tmem + kTmO + (c & 1) * 64;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        float r[32];
+        tc::tmem_ld16(tmo + lane_base + hb * 32, *reinterpret_cast<float(*)[16]>(r));
+        tc::tmem_ld16(tmo + lane_base + hb * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stage[(hb * 32 + i) * kD + dv] = from_f32<IO>(a.scale * r[i]);
+      }
+      tc::fence_before_sync();
+      mbar_arrive(&bars[kBarOFree + (c & 1)]);  // the O slot may be overwritten
+      tc::group_sync(kBarO, kGroupThreads);
+      if (ot == 0 && c + 3 < nchunks) issue_kqp(c + 3);  // every MMA of chunk c is done
+      const int t0 = c * kC;
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {  // 64 rows x 256 B = 1024 16-byte pieces
+        const int piece = rr * kGroupThreads + ot;
+        const int i = piece >> 4, col = (piece & 15) * 8;
+        if (t0 + i < T) {
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + i * kD + col);
+          *reinterpret_cast<uint4*>(o + ((static_cast<int64_t>(b) * T + t0 + i) * a.Hv + h) * kD + col) = v;
+        }
+      }
+      tc::group_sync(kBarO, kGroupThreads);  // the staging tile is reused
+      return true;
+    };
+    // Q <- diag(gamma) Q in place: thread = (row, d_k block), 8 pieces of 8
+    // elements.  Runs one chunk ahead of the state chain.
+    auto scale_q = [&](int c) -> bool {
+      if (!group_wait(&bars[kBarKQP + c % 3], (c / 3) & 1, kBarO, kGroupThreads)) return false;
+      const float* gam = pvec(c);
+      const int row = ot >> 1, blk = ot & 1;
+      const float gr = gam[row];
+      const uint32_t base = sb + kKQ + (c % 3) * kKQSlot + blk * kKQBlock + 8192;
+#pragma unroll
+      for (int pc = 0; pc < 8; ++pc) {
+        const uint32_t addr = base + tc::sw128_offset(row, pc);
+        uint32_t w[4];
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "r"(addr));
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = tc::pack2<BF16>(gr * tc::unpack_lo<BF16>(w[e]), gr * tc::unpack_hi<BF16>(w[e]));
+        tc::sts128(addr, w[0], w[1], w[2], w[3]);
+      }
+      tc::fence_proxy_async();
+      mbar_arrive(&bars[kBarQ + c % 3]);
+      return true;
+    };
+    bool ok = nchunks == 0 || scale_q(0);
+    for (int c = 0; c < nchunks && ok; ++c) {
+      if (c + 1 < nchunks && !scale_q(c + 1)) { ok = false; break; }
+      if (c >= 1 && !outputs(c - 1)) { ok = false; break; }
+      TRACE(c, 3);
+    }
+    if (ok && nchunks > 0) ok = outputs(nchunks - 1);
+    if (!ok && ot == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   } else {
     // ================================================================ state
     asm volatile("setmaxnreg.inc.sync.aligned.u32 168;" ::: "memory");
-    const int st = tid - kIntraThreads;  // 0..255
-    const int quarter = warp & 3, half = (warp - kIntraThreads / 32) >> 2;
+    const int st = tid - 2 * kGroupThreads;  // 0..255
+    const int quarter = warp & 3, half = (warp - 8) >> 2;
     const int dv = quarter * 32 + lane;
     const int k0 = half * 64;
     const size_t state_off = static_cast<size_t>(bh) * kD * kD;
-    IO* o = static_cast<IO*>(a.o);
     float S[64];
 #pragma unroll
     for (int j = 0; j < 64; ++j)
@@ -515,51 +739,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tmem_wait_st();
       tc::fence_before_sync();
     };
-    // outputs o[t0 + i][dv] = scale (gamma_i Z[dv][i] + O_intra[dv][i]): staged
-    // as a [64][128] tile in the V''hi buffer (free between the previous
-    // chunk's last MMA and this chunk's V'' epilogue), then written with
-    // coalesced 16-byte stores
-    auto outputs = [&](int c) {
-      const float* sGam = vec + (c % 3) * kVecSlot + 64;
-      IO* stage = reinterpret_cast<IO*>(smem + kVH);
-      float z[32], oi[32];
-      tc::tmem_ld16(tmem + lane_base + kTmZ + half * 32, *reinterpret_cast<float(*)[16]>(z));
-      tc::tmem_ld16(tmem + lane_base + kTmZ + half * 32 + 16, *reinterpret_cast<float(*)[16]>(z + 16));
-      tc::tmem_ld16(tmem + lane_base + kTmOI + half * 32, *reinterpret_cast<float(*)[16]>(oi));
-      tc::tmem_ld16(tmem + lane_base + kTmOI + half * 32 + 16, *reinterpret_cast<float(*)[16]>(oi + 16));
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int i = half * 32 + jj;
-        stage[i * kD + dv] = from_f32<IO>(a.scale * fmaf(sGam[i], z[jj], oi[jj]));
-      }
-      tc::fence_before_sync();
-      tc::group_sync(kBarState, kStateThreads);
-      const int t0 = c * kC;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {  // 64 rows x 256 B = 1024 16-byte pieces
-        const int piece = r * kStateThreads + st;
-        const int i = piece >> 4, col = (piece & 15) * 8;
-        if (t0 + i < T) {
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + i * kD + col);
-          *reinterpret_cast<uint4*>(o + ((static_cast<int64_t>(b) * T + t0 + i) * a.Hv + h) * kD + col) = v;
-        }
-      }
-    };
     write_st();
     tc::group_sync(kBarState, kStateThreads);
-    uint32_t x_phase = 0, z_phase = 0, s2_phase = 0;
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c & 1;
-      const float* sG = vec + (c % 3) * kVecSlot;
-      const float* sGam = sG + 64;
-      const float* sDecay = sG + 192;
-      const uint32_t kq = sb + kKQ + slot * kKQSlot;
-      const uint32_t pt = sb + kP + slot * kPSlot;
+      const uint32_t kq = sb + kKQ + (c % 3) * kKQSlot;
+      const uint32_t pt = sb + kP + (c % 3) * kPSlot;
       const uint32_t tmu = tmem + kTmU + slot * 64;
+      const uint32_t tmo = tmem + kTmO + slot * 64;
       if (!group_wait(&bars[kBarReady + slot], (c >> 1) & 1, kBarState, kStateThreads)) { ok = false; break; }
-      TRACE(c, 7);
+      TRACE(c, 4);
       if (st == 0) {  // V'^T = U^T - S^T W^T  (A = S^T from TMEM, negated)
         tc::fence_after_sync();
 #pragma unroll
@@ -567,36 +757,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mma_tmem_a(tmu, tmem + kTmST + s * 8, tc::mnmajor_desc(sb + kWT, 8192, s), kIdXneg, true);
         tc::commit(&bars[kBarX]);
       }
-      if (c >= 1) {  // outputs of the previous chunk overlap the V' MMA
-        if (!group_wait(&bars[kBarZ], z_phase, kBarState, kStateThreads)) { ok = false; break; }
-        z_phase ^= 1;
-        tc::fence_after_sync();
-        outputs(c - 1);
-      }
-      tc::group_sync(kBarState, kStateThreads);
-      if (st == 0) {  // Z^T = S^T Q^T
+      // O^T = S^T (diag(gamma) Q)^T queues behind X: it needs the scaled Q and
+      // this O slot read out (chunk c - 2)
+      if (!group_wait(&bars[kBarQ + c % 3], (c / 3) & 1, kBarState, kStateThreads)) { ok = false; break; }
+      TRACE(c, 9);
+      if (c >= 2 && !group_wait(&bars[kBarOFree + slot], ((c - 2) >> 1) & 1, kBarState, kStateThreads)) { ok = false; break; }
+      if (st == 0) {
         tc::fence_after_sync();
 #pragma unroll
         for (int s = 0; s < 8; ++s)
-          tc::mma_tmem_a(tmem + kTmZ, tmem + kTmST + s * 8, tc::kmajor_desc(kq + 8192, kKQBlock, s),
-                         kIdKQ, s > 0);
-        tc::commit(&bars[kBarZ]);
+          tc::mma_tmem_a(tmo, tmem + kTmST + s * 8, tc::kmajor_desc(kq + 8192, kKQBlock, s), kIdKQ, s > 0);
       }
-      if (!group_wait(&bars[kBarX], x_phase, kBarState, kStateThreads)) { ok = false; break; }
-      x_phase ^= 1;
+      TRACE(c, 10);
+      const float* vc = pvec(c);
+      const float gC = vc[kC - 1];
+      if (!group_wait(&bars[kBarX], c & 1, kBarState, kStateThreads)) { ok = false; break; }
       tc::fence_after_sync();
-      TRACE(c, 8);
-      {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> hi / lo tiles
+      TRACE(c, 5);
+      {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> bf16 hi / lo into TMEM
         float u[32];
         tc::tmem_ld16(tmu + lane_base + half * 32, *reinterpret_cast<float(*)[16]>(u));
         tc::tmem_ld16(tmu + lane_base + half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
         tc::tmem_wait_ld();
+        uint32_t wh[16], wl[16];
 #pragma unroll
         for (int cb = 0; cb < 2; ++cb) {
-          // each pair is converted once; the packed hi word is reused for the
-          // tile and unpacked for the lo residual
-          uint32_t wp[8], wh[8], wl[8];
-          const float4* dec4 = reinterpret_cast<const float4*>(sDecay + half * 32 + cb * 16);
+          uint32_t wp[8];
+          const float4* dec4 = reinterpret_cast<const float4*>(vc + 64 + half * 32 + cb * 16);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             const float4 d = dec4[q4];
@@ -607,49 +794,47 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float u0 = u[cb * 16 + 2 * e], u1 = u[cb * 16 + 2 * e + 1];
               const float v0 = u0 * dd[2 * e2], v1 = u1 * dd[2 * e2 + 1];
               wp[e] = tc::pack2<BF16>(u0, u1);
-              wh[e] = tc::pack2<BF16>(v0, v1);
-              wl[e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(wh[e]), v1 - tc::unpack_hi<BF16>(wh[e]));
+              const uint32_t hw = tc::pack2<BF16>(v0, v1);
+              wh[cb * 8 + e] = hw;
+              wl[cb * 8 + e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(hw), v1 - tc::unpack_hi<BF16>(hw));
             }
           }
           const int ch = half * 4 + cb * 2;
 #pragma unroll
-          for (int k2 = 0; k2 < 2; ++k2) {
+          for (int k2 = 0; k2 < 2; ++k2)
             tc::sts128(sb + kVP + tc::sw128_offset(dv, ch + k2), wp[4 * k2], wp[4 * k2 + 1],
                        wp[4 * k2 + 2], wp[4 * k2 + 3]);
-            tc::sts128(sb + kVH + tc::sw128_offset(dv, ch + k2), wh[4 * k2], wh[4 * k2 + 1],
-                       wh[4 * k2 + 2], wh[4 * k2 + 3]);
-            tc::sts128(sb + kVL + tc::sw128_offset(dv, ch + k2), wl[4 * k2], wl[4 * k2 + 1],
-                       wl[4 * k2 + 2], wl[4 * k2 + 3]);
-          }
         }
+        // every thread of this lane has read its V' columns before any overwrite
+        tc::group_sync(kBarState, kStateThreads);
+        tc::tmem_st16(tmu + lane_base + half * 16, wh);
+        tc::tmem_st16(tmu + lane_base + 32 + half * 16, wl);
+        tc::tmem_wait_st();
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
       tc::group_sync(kBarState, kStateThreads);
-      TRACE(c, 9);
-      if (st == 0) {  // O_intra^T = V'^T P^T ; dS^T = V''hi^T K + V''lo^T K
+      TRACE(c, 6);
+      if (st == 0) {  // dS^T = V''hi^T K + V''lo^T K (A from TMEM), then O^T += V'^T P^T
         tc::fence_after_sync();
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          tc::mma(tmem + kTmOI, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(pt, 0, s), kIdKQ, s > 0);
+          tc::mma_tmem_a(tmem + kTmDS, tmu + s * 8, tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, s > 0);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVH, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
-                  s > 0);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma(tmem + kTmDS, tc::kmajor_desc(sb + kVL, 0, s), tc::mnmajor_desc(kq, kKQBlock, s), kIdDS,
-                  true);
+          tc::mma_tmem_a(tmem + kTmDS, tmu + 32 + s * 8, tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, true);
         tc::commit(&bars[kBarS2]);
-        tc::commit(&bars[kBarSlotFree + slot]);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma(tmo, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(pt, 0, s), kIdKQ, true);
+        tc::commit(&bars[kBarZO + slot]);
       }
-      if (!group_wait(&bars[kBarS2], s2_phase, kBarState, kStateThreads)) { ok = false; break; }
-      s2_phase ^= 1;
+      // dS done; so is the S^T Q^T product (issued earlier: tcgen05 operations
+      // of one thread complete in order), which read the old S^T
+      if (!group_wait(&bars[kBarS2], c & 1, kBarState, kStateThreads)) { ok = false; break; }
       tc::fence_after_sync();
-      if (st == 0 && c + 2 < nchunks) issue_tma(c + 2);  // this slot's MMAs are done
-      TRACE(c, 10);
+      TRACE(c, 7);
       {  // S <- gamma_C S + dS ; bf16 S^T back into TMEM for the next chunk
-        const float gC = sGam[kC - 1];
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
           float r[32];
@@ -663,23 +848,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         write_st();
       }
       tc::group_sync(kBarState, kStateThreads);
-      TRACE(c, 11);
+      TRACE(c, 8);
     }
     if (ok && nchunks > 0) {
-      if (group_wait(&bars[kBarZ], z_phase, kBarState, kStateThreads)) {
-        tc::fence_after_sync();
-        outputs(nchunks - 1);
 #pragma unroll
-        for (int j = 0; j < 64; ++j)
-          a.final_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] = S[j];
-      } else {
-        ok = false;
-      }
+      for (int j = 0; j < 64; ++j)
+        a.final_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] = S[j];
     }
-    if (!ok && st == 0) {
-      report(a.status, GDN_DEVERR_MMA_TIMEOUT);
-      *abort_flag = 1;
-    }
+    if (!ok && st == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   }
 
   tc::fence_before_sync();
@@ -687,16 +863,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
 }
 
+size_t workspace_bytes(const gdn_prefill_args_t& a) {
+  const size_t nchunks = (static_cast<size_t>(a.T) + kC - 1) / kC;
+  return static_cast<size_t>(a.B) * a.Hv * nchunks * kWsUnit;
+}
+
 template <bool BF16>
 int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
-  static std::atomic<uint64_t> attr_done{0};
+  static std::atomic<uint64_t> attr_intra{0}, attr_state{0};
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  if (static_cast<int>(kSmemAlloc) > di.smem_optin) return GDN_ERR_SHAPE;
-  auto kern = prefill_kernel<BF16>;
-  rc = ensure_smem_attr(kern, kSmemAlloc, attr_done);
-  if (rc) return rc;
+  if (static_cast<int>(state::kSmemAlloc) > di.smem_optin) return GDN_ERR_SHAPE;
+  auto k1 = intra_kernel<BF16>;
+  auto k2 = state_kernel<BF16>;
+  if ((rc = ensure_smem_attr(k1, intra::kSmemAlloc, attr_intra))) return rc;
+  if ((rc = ensure_smem_attr(k2, state::kSmemAlloc, attr_state))) return rc;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
   const uint32_t box[4] = {64, 1, kC, 1};
@@ -719,7 +901,11 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   p.a = a;
   p.nchunks = (a.T + kC - 1) / kC;
   p.group = a.Hv / a.Hqk;
-  kern<<<static_cast<unsigned>(a.B * a.Hv), kThreads, kSmemAlloc, stream>>>(p, mq, mk, mv);
+  p.ws = static_cast<unsigned char*>(a.workspace);
+  const unsigned n1 = static_cast<unsigned>(a.B * a.Hqk * p.nchunks);
+  k1<<<n1, intra::kThreads, intra::kSmemAlloc, stream>>>(p, mq, mk);
+  if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+  k2<<<static_cast<unsigned>(a.B * a.Hv), state::kThreads, state::kSmemAlloc, stream>>>(p, mq, mk, mv);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
@@ -728,12 +914,17 @@ int validate(const gdn_prefill_args_t* a) {
   if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->final_state || !a->o) return GDN_ERR_NULL;
   if (a->B < 1 || a->T < 1 || a->Hqk < 1 || a->Hv < 1 || a->Hv % a->Hqk) return GDN_ERR_SHAPE;
   if (a->dk != kD || a->dv != kD || a->chunk != kC) return GDN_ERR_SHAPE;
-  if (static_cast<int64_t>(a->B) * a->Hv > 0x7FFFFFFF) return GDN_ERR_SHAPE;
+  const int64_t nchunks = (static_cast<int64_t>(a->T) + kC - 1) / kC;
+  if (static_cast<int64_t>(a->B) * a->Hv > 0x7FFFFFFF ||
+      static_cast<int64_t>(a->B) * a->Hqk * nchunks > 0x7FFFFFFF)
+    return GDN_ERR_SHAPE;
   if (a->io_dtype != GDN_DT_BF16 && a->io_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
   if (!dtype_valid(a->g_dtype) || !dtype_valid(a->beta_dtype)) return GDN_ERR_DTYPE;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) ||
       !aligned16(a->final_state) || (a->initial_state && !aligned16(a->initial_state)))
     return GDN_ERR_ALIGN;
+  if (!a->workspace || a->workspace_bytes < workspace_bytes(*a)) return GDN_ERR_WORKSPACE;
+  if (!aligned16(a->workspace)) return GDN_ERR_ALIGN;
   return GDN_OK;
 }
 
@@ -749,7 +940,10 @@ extern "C" int gdn_prefill_trace_read(unsigned long long* host) {
 }
 #endif
 
-extern "C" size_t gdn_prefill_workspace_size(const gdn_prefill_args_t*) { return 0; }
+extern "C" size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args) {
+  if (!args || args->B < 1 || args->T < 1 || args->Hv < 1) return 0;
+  return gdn::prefill::workspace_bytes(*args);
+}
 
 extern "C" int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream) {
   int rc = gdn::prefill::validate(args);
