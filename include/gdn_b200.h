@@ -134,8 +134,9 @@ typedef struct {
  * initial_state may be NULL (zero state).  final_state receives the state
  * after token T-1.  chunk must be 64; T may be any length >= 1 (the last
  * chunk is zero-padded, which leaves state and outputs unchanged).
- * d_k = d_v = 128.  No workspace is needed (gdn_prefill_workspace_size
- * returns 0).
+ * d_k = d_v = 128.  The prefill needs a device workspace of
+ * gdn_prefill_workspace_size(args) bytes (16-byte aligned), owned by the
+ * caller and passed in `workspace`.
  */
 typedef struct {
   const void* q;            /* [B, T, Hqk, d_k] io_dtype                    */
