@@ -37,6 +37,7 @@ EXPORTED = (
     "kda_decode_ref_launch",
     "gdn_prefill_workspace_size",
     "gdn_prefill_launch",
+    "gdn_prefill_launch_noalloc",
     "kda_prefill_launch",
     "gdn_ipc_handle",
     "gdn_ipc_open",
@@ -136,6 +137,8 @@ def load(path: str | Path | None = None):
         L.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         L.gdn_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
         L.gdn_prefill_launch.restype = ctypes.c_int
+        L.gdn_prefill_launch_noalloc.argtypes = [ctypes.POINTER(PrefillArgs), vp]
+        L.gdn_prefill_launch_noalloc.restype = ctypes.c_int
         L.kda_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
         L.kda_prefill_launch.restype = ctypes.c_int
         L.gdn_ipc_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]

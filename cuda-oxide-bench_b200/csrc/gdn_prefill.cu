@@ -42,6 +42,7 @@
 
 #include <atomic>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -953,4 +954,54 @@ extern "C" int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t s
   auto s = reinterpret_cast<cudaStream_t>(stream);
   return args->io_dtype == GDN_DT_BF16 ? gdn::prefill::launch<true>(*args, s)
                                        : gdn::prefill::launch<false>(*args, s);
+}
+
+// ------------------------------------------------------------------------
+// gdn_prefill_launch_noalloc: the same two kernels, with their workspace in a
+// fixed device array instead of caller-provided memory, for callers that
+// cannot allocate device memory themselves (see include/gdn_b200.h).
+// The array is a module global: every GPU that loads this library holds
+// GDN_PREFILL_NOALLOC_SCRATCH_BYTES of it until the process exits, and all
+// calls on a device share it.  Host code must not pass the symbol itself to a
+// kernel (on the host it names a host-side stand-in); its device address is
+// looked up once per device with cudaGetSymbolAddress, with that device
+// current, on the first call there.
+namespace {
+
+static __device__ __align__(256) unsigned char g_prefill_noalloc_scratch[GDN_PREFILL_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};  // device address of the array, per device ordinal
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_prefill_noalloc_scratch) != cudaSuccess || !p) return GDN_ERR_DEVICE;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GDN_OK;
+}
+
+}  // namespace
+
+static_assert(gdn::prefill::kWsUnit == GDN_PREFILL_WS_RECORD_BYTES, "record size in the header");
+
+extern "C" int gdn_prefill_launch_noalloc(const gdn_prefill_args_t* args, gdn_stream_t stream) {
+  if (!args) return GDN_ERR_NULL;
+  if (args->B < 1 || args->T < 1 || args->Hv < 1) return GDN_ERR_SHAPE;
+  gdn_prefill_args_t a = *args;
+  // One record per (sequence, value head, 64-token chunk); nothing in the
+  // scratch has to start at zero: the first kernel writes every record the
+  // second one reads, in stream order.
+  if (gdn::prefill::workspace_bytes(a) > GDN_PREFILL_NOALLOC_SCRATCH_BYTES) return GDN_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  a.workspace = scratch;
+  a.workspace_bytes = GDN_PREFILL_NOALLOC_SCRATCH_BYTES;
+  return gdn_prefill_launch(&a, stream);
 }

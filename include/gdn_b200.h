@@ -217,6 +217,36 @@ size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args);
 int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
 /*
+ * GDN chunked prefill that allocates nothing.  No counterpart in the
+ * reference: this entry point exists for callers of this library that
+ * cannot allocate device memory themselves — for example a plugin inside a
+ * host framework that owns the GPU memory pool and exposes no allocator to
+ * it, or a caller that must not trigger cudaMalloc's implicit device
+ * synchronisation on its serving path.  Such a caller still passes its
+ * inputs and outputs (args->workspace and args->workspace_bytes are ignored);
+ * the workspace gdn_prefill_launch would take lives instead in a fixed
+ * device array of GDN_PREFILL_NOALLOC_SCRATCH_BYTES inside this library,
+ * which every GPU that loads the library holds until the process exits.
+ *   - Limit: one record of GDN_PREFILL_WS_RECORD_BYTES per (sequence, value
+ *     head, 64-token chunk), i.e. B * Hv * ceil(T / 64) <= 668 (for example
+ *     one sequence of 32 value heads up to T = 1344).  Larger problems return
+ *     GDN_ERR_WORKSPACE without launching anything.
+ *   - Set-up: the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current) and caches it; make
+ *     that first call before any stream capture on the device.  No call
+ *     allocates device memory (no cudaMalloc, cudaFree or allocating library
+ *     routine).
+ *   - Sharing: every call on a device uses the same array, which keeps the
+ *     last call's contents (nothing in it needs to start at zero).  Calls
+ *     whose kernels overlap on the GPU (two streams, or two host threads)
+ *     race on it: order them on one stream or serialise them.
+ * Results equal gdn_prefill_launch's on the same arguments.
+ */
+#define GDN_PREFILL_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+#define GDN_PREFILL_WS_RECORD_BYTES 25088u
+int gdn_prefill_launch_noalloc(const gdn_prefill_args_t* args, gdn_stream_t stream);
+
+/*
  * KDA prefill: T applications of the reference's per-channel-gate step
  * naive_recurrent_kda_step
  * (analysis/wave15-attention-architecture/reference/pytorch_reference_kda.py:42-71),
