@@ -113,9 +113,10 @@ __device__ __forceinline__ void store_row16_global(unsigned char* tile, int row,
 // barrier instead of competing for issue slots), then a group-wide vote: the
 // group leaves together if any warp timed out (no thread is stranded at a
 // barrier).  The barrier also orders the waiters' later reads after the phase.
-__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int bar_id, int count) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity);
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int bar_id, int count,
+                                           bool failed = false) {
+  bool ok = !failed;
+  if ((threadIdx.x & 31) == 0 && ok) ok = mbar_wait_bounded(bar, parity);
   return !named_barrier_or(bar_id, count, !ok);
 }
 
@@ -486,20 +487,24 @@ constexpr uint32_t kV = 126976;      // V tile: 2 d_v blocks x 8 KB (one slot)
 constexpr uint32_t kVBlock = 8192;
 constexpr uint32_t kTw = 143360;     // T_w tile (8 KB), then T_u (8 KB): one slot
 constexpr uint32_t kTu = 151552;
-constexpr uint32_t kWT = 159744;     // W^T, MN-major rows d_k               (16 KB)
-constexpr uint32_t kVP = 176128;     // V'^T, K-major rows d_v               (16 KB)
-constexpr uint32_t kOut = 192512;    // output staging [64][128] io          (16 KB)
-constexpr uint32_t kBars = 208896;
+constexpr uint32_t kWQ = 159744;     // W^T, then 2 slots of (diag(gamma) Q)^T: MN-major rows
+                                     // d_k, 64 tokens each (16 KB per tile).  W^T and the Q^T
+                                     // tile of a chunk form one N = 128 operand whose second
+                                     // 64-token block sits 16 KB (slot 0) or 32 KB (slot 1) on
+constexpr uint32_t kVP = 208896;     // V'^T, K-major rows d_v               (16 KB)
+constexpr uint32_t kBars = 225280;
 constexpr uint32_t kSmemBytes = kBars + 256;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 static_assert(kP % 1024 == 0 && kPSlot % 1024 == 0 && kV % 1024 == 0 && kTw % 1024 == 0 &&
-              kWT % 1024 == 0 && kVP % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+              kWQ % 1024 == 0 && kVP % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
 // TMEM columns
 constexpr uint32_t kTmST = 0;    // S^T bf16, packed pairs: 64 columns
 constexpr uint32_t kTmW = 64;    // W^T
-constexpr uint32_t kTmU = 128;   // 2 slots x U^T / V'^T, then V''^T hi | lo (bf16 pairs)
-constexpr uint32_t kTmO = 256;   // 2 slots x O^T = S^T (diag(gamma) Q)^T + V'^T P^T
+// 2 slots of 128 columns, each [U^T | O^T]: U^T / V'^T (later V''^T hi | lo as
+// bf16 pairs) and the negated output O^T = -(S^T (diag(gamma) Q)^T + V'^T P^T),
+// adjacent so that one N = 128 product updates both
+constexpr uint32_t kTmUO = 128;
 constexpr uint32_t kTmDS = 384, kTmCols = 512;
 
 // mbarrier indices
@@ -507,13 +512,14 @@ enum {
   kBarKQP = 0,     // [3] K, Q (TMA), P and the vectors (bulk) of a chunk landed
   kBarTWU = 3,     // V (TMA), T_w | T_u (bulk) of a chunk landed
   kBarHMma = 4,    // W/U MMAs completed
-  kBarReady = 5,   // [2] W group -> state: W^T tile and U of a chunk ready
-  kBarQ = 7,       // [3] O group -> state: Q of a chunk scaled by gamma (by K/Q/P slot)
-  kBarOFree = 10,  // [2] O group finished reading an O slot
-  kBarX = 12,      // V' = U - W S done
-  kBarS2 = 13,     // dS done
-  kBarZO = 14,     // [2] O of a chunk complete (its K/Q/P slot is free)
-  kNumBars = 16,
+  kBarGo = 5,      // [2] W and O groups -> state: the [W^T | Q^T] tile and U of a
+                   //     chunk are ready, and its O slot is clear
+  kBarTiles = 7,   // state threads -> MMA thread: V'^T tile and V'' hi / lo written
+  kBarSt = 8,      // state threads -> MMA thread: bf16 S^T of the next chunk written
+  kBarX = 9,       // V' = U - W S (and the first O term) done
+  kBarS2 = 10,     // dS done
+  kBarZO = 11,     // [2] O of a chunk complete (its K/Q/P slot is free)
+  kNumBars = 13,
 };
 }  // namespace state
 
@@ -552,11 +558,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     for (int i = 0; i < 3; ++i) mbar_init(&bars[kBarKQP + i], 1);
     mbar_init(&bars[kBarTWU], 1);
     mbar_init(&bars[kBarHMma], 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[kBarReady + i], kGroupThreads);
-      mbar_init(&bars[kBarOFree + i], kGroupThreads);
-    }
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[kBarQ + i], kGroupThreads);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars[kBarGo + i], 2 * kGroupThreads);
+    mbar_init(&bars[kBarTiles], kStateThreads);
+    mbar_init(&bars[kBarSt], kStateThreads);
     mbar_init(&bars[kBarX], 1);
     mbar_init(&bars[kBarS2], 1);
     mbar_init(&bars[kBarZO], 1);
@@ -568,9 +572,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
   const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-  constexpr uint32_t kIdKQ = tc::idesc_f16(128, 64, false, false, BF16);
   constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, BF16);
-  constexpr uint32_t kIdXneg = tc::idesc_f16(128, 64, false, true, BF16, true);
+  constexpr uint32_t kIdXZ = tc::idesc_f16(128, 128, false, true, BF16, true);
+  constexpr uint32_t kIdOIneg = tc::idesc_f16(128, 64, false, false, BF16, true);
   constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, BF16);
 
   auto issue_kqp = [&](int n) {  // K, Q (TMA), P and vectors (bulk) of chunk n into slot n % 3
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c & 1;
       const uint32_t kq = sb + kKQ + (c % 3) * kKQSlot;
-      const uint32_t tmu = tmem + kTmU + slot * 64;
+      const uint32_t tmu = tmem + kTmUO + slot * 128;
       if (!group_wait(&bars[kBarKQP + c % 3], (c / 3) & 1, kBarW, kGroupThreads)) { ok = false; break; }
       if (!group_wait(&bars[kBarTWU], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
       // the U slot was last used by chunk c - 2 (its dS MMA precedes X of c - 1)
@@ -637,12 +641,12 @@ __global__ void __launch_bounds__(state::kThreads, 1)
         tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32, *reinterpret_cast<float(*)[16]>(r));
         tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
         tc::tmem_wait_ld();
-        store_row16<BF16>(sb + kWT, k, ih * 4, r);
-        store_row16<BF16>(sb + kWT, k, ih * 4 + 2, r + 16);
+        store_row16<BF16>(sb + kWQ, k, ih * 4, r);
+        store_row16<BF16>(sb + kWQ, k, ih * 4 + 2, r + 16);
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
-      mbar_arrive(&bars[kBarReady + slot]);
+      mbar_arrive(&bars[kBarGo + slot]);
       TRACE(c, 2);
     }
     if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
@@ -652,70 +656,97 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     const int ot = tid - kGroupThreads;  // 0..127
     const int dv = (warp & 3) * 32 + lane;
     IO* o = static_cast<IO*>(a.o);
-    // outputs o[t0 + i][dv] = scale O[dv][i]: staged as a [64][128] tile, then
-    // written with coalesced 16-byte stores; the slot of chunk c is then
-    // refilled with chunk c + 3
+    auto zero_o = [&](int slot) {  // the O product of the next chunk in this slot starts from 0
+      uint32_t z[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) z[e] = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tc::tmem_st16(tmem + kTmUO + slot * 128 + 64 + lane_base + q * 16, z);
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+    };
+    // (diag(gamma) Q)^T of chunk c into Q^T slot c & 1: 8 x 8 blocks moved
+    // with ldmatrix.trans / stmatrix.  Warp w handles d_k blocks 4w..4w+3,
+    // four 8-token blocks per instruction.
+    auto scale_q = [&](int c) -> bool {
+      if (!group_wait(&bars[kBarKQP + c % 3], (c / 3) & 1, kBarO, kGroupThreads)) return false;
+      const float* gam = pvec(c);
+      const int w = warp & 3, m = lane >> 3, r8 = lane & 7;
+      const uint32_t qslot = sb + kKQ + (c % 3) * kKQSlot + 8192;
+      const uint32_t qt = sb + kWQ + 16384 * (1 + (c & 1));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kc = w * 4 + j;  // d_k rows 8 kc .. 8 kc + 7 (K block kc / 8)
+        const uint32_t src = qslot + (kc >> 3) * kKQBlock;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t v[4];
+          tc::ldsm_x4_trans(src + tc::sw128_offset(8 * (4 * hh + m) + r8, kc & 7), v);
+#pragma unroll
+          for (int mm = 0; mm < 4; ++mm) {
+            const float2 g2 = *reinterpret_cast<const float2*>(gam + 8 * (4 * hh + mm) + 2 * (lane & 3));
+            v[mm] = tc::pack2<BF16>(g2.x * tc::unpack_lo<BF16>(v[mm]), g2.y * tc::unpack_hi<BF16>(v[mm]));
+          }
+          tc::stsm_x4(qt + tc::sw128_offset(8 * kc + r8, 4 * hh + m), v);
+        }
+      }
+      tc::fence_proxy_async();
+      return true;
+    };
+    // outputs o[t0 + i][dv] = -scale O[dv][i] (O holds the negated product)
+    // of chunk c, after which the O slot is cleared and the go of chunk c + 2
+    // (its scaled Q^T tile and this cleared slot) is announced.  The outputs
+    // are staged, row-major, in the Q tile of K/Q/P slot (c + 2) % 3, which is
+    // no longer needed once its scaled copy exists (or holds the finished
+    // chunk c - 1), and then written with coalesced 16-byte stores.
     auto outputs = [&](int c) -> bool {
       if (!group_wait(&bars[kBarZO + (c & 1)], (c >> 1) & 1, kBarO, kGroupThreads)) return false;
       tc::fence_after_sync();
-      IO* stage = reinterpret_cast<IO*>(smem + kOut);
-      const uint32_t tmo = tmem + kTmO + (c & 1) * 64;
+      if (ot == 0 && c + 3 < nchunks) issue_kqp(c + 3);  // every MMA of chunk c is done
+      if (c + 2 < nchunks && !scale_q(c + 2)) return false;
+      tc::group_sync(kBarO, kGroupThreads);  // every warp has read the Q tile reused below
+      const uint32_t tmo = tmem + kTmUO + (c & 1) * 128 + 64;
+      unsigned char* stage = smem + kKQ + ((c + 2) % 3) * kKQSlot + 8192;  // + (dv / 64) * kKQBlock
+      const float ns = -a.scale;
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         float r[32];
         tc::tmem_ld16(tmo + lane_base + hb * 32, *reinterpret_cast<float(*)[16]>(r));
         tc::tmem_ld16(tmo + lane_base + hb * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
         tc::tmem_wait_ld();
+        if (hb == 1) {
+          zero_o(c & 1);
+          mbar_arrive(&bars[kBarGo + (c & 1)]);  // go of chunk c + 2
+        }
+        IO* st_col = reinterpret_cast<IO*>(stage + (dv >> 6) * kKQBlock) + (dv & 63);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) stage[(hb * 32 + i) * kD + dv] = from_f32<IO>(a.scale * r[i]);
+        for (int i = 0; i < 32; ++i) st_col[(hb * 32 + i) * 64] = from_f32<IO>(ns * r[i]);
       }
-      tc::fence_before_sync();
-      mbar_arrive(&bars[kBarOFree + (c & 1)]);  // the O slot may be overwritten
       tc::group_sync(kBarO, kGroupThreads);
-      if (ot == 0 && c + 3 < nchunks) issue_kqp(c + 3);  // every MMA of chunk c is done
       const int t0 = c * kC;
 #pragma unroll
       for (int rr = 0; rr < 8; ++rr) {  // 64 rows x 256 B = 1024 16-byte pieces
         const int piece = rr * kGroupThreads + ot;
         const int i = piece >> 4, col = (piece & 15) * 8;
         if (t0 + i < T) {
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + i * kD + col);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + (col >> 6) * kKQBlock + i * 128 + (col & 63) * 2);
           *reinterpret_cast<uint4*>(o + ((static_cast<int64_t>(b) * T + t0 + i) * a.Hv + h) * kD + col) = v;
         }
       }
-      tc::group_sync(kBarO, kGroupThreads);  // the staging tile is reused
+      tc::group_sync(kBarO, kGroupThreads);  // the staging tile may be refilled
       return true;
     };
-    // Q <- diag(gamma) Q in place: thread = (row, d_k block), 8 pieces of 8
-    // elements.  Runs one chunk ahead of the state chain.
-    auto scale_q = [&](int c) -> bool {
-      if (!group_wait(&bars[kBarKQP + c % 3], (c / 3) & 1, kBarO, kGroupThreads)) return false;
-      const float* gam = pvec(c);
-      const int row = ot >> 1, blk = ot & 1;
-      const float gr = gam[row];
-      const uint32_t base = sb + kKQ + (c % 3) * kKQSlot + blk * kKQBlock + 8192;
-#pragma unroll
-      for (int pc = 0; pc < 8; ++pc) {
-        const uint32_t addr = base + tc::sw128_offset(row, pc);
-        uint32_t w[4];
-        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "r"(addr));
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          w[e] = tc::pack2<BF16>(gr * tc::unpack_lo<BF16>(w[e]), gr * tc::unpack_hi<BF16>(w[e]));
-        tc::sts128(addr, w[0], w[1], w[2], w[3]);
-      }
-      tc::fence_proxy_async();
-      mbar_arrive(&bars[kBarQ + c % 3]);
-      return true;
-    };
-    bool ok = nchunks == 0 || scale_q(0);
+    zero_o(0);
+    zero_o(1);
+    bool ok = true;
+    for (int c = 0; c < 2 && c < nchunks && ok; ++c) {
+      ok = scale_q(c);
+      if (ok) mbar_arrive(&bars[kBarGo + c]);
+    }
     for (int c = 0; c < nchunks && ok; ++c) {
-      if (c + 1 < nchunks && !scale_q(c + 1)) { ok = false; break; }
-      if (c >= 1 && !outputs(c - 1)) { ok = false; break; }
+      if (!outputs(c)) { ok = false; break; }
       TRACE(c, 3);
     }
-    if (ok && nchunks > 0) ok = outputs(nchunks - 1);
     if (!ok && ot == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   } else {
     // ================================================================ state
@@ -742,48 +773,46 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     };
     write_st();
     tc::group_sync(kBarState, kStateThreads);
+    // Only the MMA thread (st == 0) waits for the other groups and for the
+    // state threads' writes (mbarriers); all threads meet in a barrier vote
+    // only where they need an MMA result (X and dS), and the MMA thread joins
+    // those votes with its own waits' outcome.
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c & 1;
       const uint32_t kq = sb + kKQ + (c % 3) * kKQSlot;
       const uint32_t pt = sb + kP + (c % 3) * kPSlot;
-      const uint32_t tmu = tmem + kTmU + slot * 64;
-      const uint32_t tmo = tmem + kTmO + slot * 64;
-      if (!group_wait(&bars[kBarReady + slot], (c >> 1) & 1, kBarState, kStateThreads)) { ok = false; break; }
-      TRACE(c, 4);
-      if (st == 0) {  // V'^T = U^T - S^T W^T  (A = S^T from TMEM, negated)
-        tc::fence_after_sync();
+      const uint32_t tmu = tmem + kTmUO + slot * 128;
+      const uint32_t tmo = tmu + 64;
+      bool mine = true;
+      if (st == 0) {  // [V'^T | O^T] = [U^T | 0] - S^T [W^T | (diag(gamma) Q)^T]  (A = S^T from TMEM)
+        mine = (c == 0 || mbar_wait_bounded(&bars[kBarSt], (c - 1) & 1)) &&
+               mbar_wait_bounded(&bars[kBarGo + slot], (c >> 1) & 1);
+        TRACE(c, 4);
+        if (mine) {
+          tc::fence_after_sync();
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          tc::mma_tmem_a(tmu, tmem + kTmST + s * 8, tc::mnmajor_desc(sb + kWT, 8192, s), kIdXneg, true);
-        tc::commit(&bars[kBarX]);
+          for (int s = 0; s < 8; ++s)
+            tc::mma_tmem_a(tmu, tmem + kTmST + s * 8, tc::mnmajor_desc(sb + kWQ, 16384 * (1 + slot), s),
+                           kIdXZ, true);
+          tc::commit(&bars[kBarX]);
+        }
       }
-      // O^T = S^T (diag(gamma) Q)^T queues behind X: it needs the scaled Q and
-      // this O slot read out (chunk c - 2)
-      if (!group_wait(&bars[kBarQ + c % 3], (c / 3) & 1, kBarState, kStateThreads)) { ok = false; break; }
-      TRACE(c, 9);
-      if (c >= 2 && !group_wait(&bars[kBarOFree + slot], ((c - 2) >> 1) & 1, kBarState, kStateThreads)) { ok = false; break; }
-      if (st == 0) {
-        tc::fence_after_sync();
-#pragma unroll
-        for (int s = 0; s < 8; ++s)
-          tc::mma_tmem_a(tmo, tmem + kTmST + s * 8, tc::kmajor_desc(kq + 8192, kKQBlock, s), kIdKQ, s > 0);
-      }
-      TRACE(c, 10);
       const float* vc = pvec(c);
-      const float gC = vc[kC - 1];
-      if (!group_wait(&bars[kBarX], c & 1, kBarState, kStateThreads)) { ok = false; break; }
+      if (!group_wait(&bars[kBarX], c & 1, kBarState, kStateThreads, !mine)) { ok = false; break; }
       tc::fence_after_sync();
+      const float gC = vc[kC - 1];
       TRACE(c, 5);
-      {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> bf16 hi / lo into TMEM
+      {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> bf16 hi / lo
+         // written back over the thread's own V' columns: for its 32 tokens,
+         // hi in the first 16 packed columns and lo in the next 16
         float u[32];
         tc::tmem_ld16(tmu + lane_base + half * 32, *reinterpret_cast<float(*)[16]>(u));
         tc::tmem_ld16(tmu + lane_base + half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
         tc::tmem_wait_ld();
-        uint32_t wh[16], wl[16];
 #pragma unroll
         for (int cb = 0; cb < 2; ++cb) {
-          uint32_t wp[8];
+          uint32_t wp[8], wh[8], wl[8];
           const float4* dec4 = reinterpret_cast<const float4*>(vc + 64 + half * 32 + cb * 16);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
@@ -796,8 +825,8 @@ __global__ void __launch_bounds__(state::kThreads, 1)
               const float v0 = u0 * dd[2 * e2], v1 = u1 * dd[2 * e2 + 1];
               wp[e] = tc::pack2<BF16>(u0, u1);
               const uint32_t hw = tc::pack2<BF16>(v0, v1);
-              wh[cb * 8 + e] = hw;
-              wl[cb * 8 + e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(hw), v1 - tc::unpack_hi<BF16>(hw));
+              wh[e] = hw;
+              wl[e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(hw), v1 - tc::unpack_hi<BF16>(hw));
             }
           }
           const int ch = half * 4 + cb * 2;
@@ -805,34 +834,38 @@ __global__ void __launch_bounds__(state::kThreads, 1)
           for (int k2 = 0; k2 < 2; ++k2)
             tc::sts128(sb + kVP + tc::sw128_offset(dv, ch + k2), wp[4 * k2], wp[4 * k2 + 1],
                        wp[4 * k2 + 2], wp[4 * k2 + 3]);
+          // this thread's V' columns were loaded (tcgen05.wait::ld) before the overwrite
+          tc::tmem_st8(tmu + lane_base + half * 32 + cb * 8, wh);
+          tc::tmem_st8(tmu + lane_base + half * 32 + 16 + cb * 8, wl);
         }
-        // every thread of this lane has read its V' columns before any overwrite
-        tc::group_sync(kBarState, kStateThreads);
-        tc::tmem_st16(tmu + lane_base + half * 16, wh);
-        tc::tmem_st16(tmu + lane_base + 32 + half * 16, wl);
         tc::tmem_wait_st();
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
-      tc::group_sync(kBarState, kStateThreads);
+      mbar_arrive(&bars[kBarTiles]);
       TRACE(c, 6);
-      if (st == 0) {  // dS^T = V''hi^T K + V''lo^T K (A from TMEM), then O^T += V'^T P^T
-        tc::fence_after_sync();
+      if (st == 0) {  // dS^T = V''hi^T K + V''lo^T K (A from TMEM), then O^T -= V'^T P^T
+        mine = mbar_wait_bounded(&bars[kBarTiles], c & 1);
+        if (mine) {
+          tc::fence_after_sync();
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma_tmem_a(tmem + kTmDS, tmu + s * 8, tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, s > 0);
+          for (int s = 0; s < 4; ++s)  // tokens [16 s, 16 s + 16): hi of half s / 2
+            tc::mma_tmem_a(tmem + kTmDS, tmu + (s >> 1) * 32 + (s & 1) * 8, tc::mnmajor_desc(kq, kKQBlock, s),
+                           kIdDS, s > 0);
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma_tmem_a(tmem + kTmDS, tmu + 32 + s * 8, tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, true);
-        tc::commit(&bars[kBarS2]);
+          for (int s = 0; s < 4; ++s)
+            tc::mma_tmem_a(tmem + kTmDS, tmu + (s >> 1) * 32 + 16 + (s & 1) * 8,
+                           tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, true);
+          tc::commit(&bars[kBarS2]);
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
-          tc::mma(tmo, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(pt, 0, s), kIdKQ, true);
-        tc::commit(&bars[kBarZO + slot]);
+          for (int s = 0; s < 4; ++s)
+            tc::mma(tmo, tc::kmajor_desc(sb + kVP, 0, s), tc::kmajor_desc(pt, 0, s), kIdOIneg, true);
+          tc::commit(&bars[kBarZO + slot]);
+        }
       }
-      // dS done; so is the S^T Q^T product (issued earlier: tcgen05 operations
-      // of one thread complete in order), which read the old S^T
-      if (!group_wait(&bars[kBarS2], c & 1, kBarState, kStateThreads)) { ok = false; break; }
+      // dS done, and with it the earlier X / O product that read the old S^T
+      // (tcgen05 operations of one thread complete in order)
+      if (!group_wait(&bars[kBarS2], c & 1, kBarState, kStateThreads, !mine)) { ok = false; break; }
       tc::fence_after_sync();
       TRACE(c, 7);
       {  // S <- gamma_C S + dS ; bf16 S^T back into TMEM for the next chunk
@@ -848,7 +881,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
         }
         write_st();
       }
-      tc::group_sync(kBarState, kStateThreads);
+      mbar_arrive(&bars[kBarSt]);
       TRACE(c, 8);
     }
     if (ok && nchunks > 0) {

@@ -128,6 +128,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&u)[16
       "r"(u[8]), "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
       : "memory");
 }
+// 32 lanes x 8 consecutive 32-bit columns from registers.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&u)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -195,6 +202,24 @@ template <bool BF16>
 __device__ __forceinline__ float unpack_hi(uint32_t w) {
   if (BF16) return __uint_as_float(w & 0xFFFF0000u);
   return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+
+// Four 8x8 b16 matrices from shared memory, transposed (ldmatrix .trans):
+// lane L gives the address of row L % 8 of matrix L / 8; afterwards lane t
+// holds, for each matrix m, the pair (rows 2 (t % 4), 2 (t % 4) + 1) of
+// column t / 4 packed in r[m].
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// Four 8x8 b16 matrices to shared memory (stmatrix): lane L gives the address
+// of row L % 8 of matrix L / 8; r[m] of lane t is stored to row t / 4,
+// columns 2 (t % 4) and 2 (t % 4) + 1 of matrix m.
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
