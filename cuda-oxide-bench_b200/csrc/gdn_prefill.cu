@@ -64,7 +64,16 @@ __device__ unsigned long long g_trace[64 * 16];
     if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x & 127) == 0 && threadIdx.x < 384)        \
       g_trace[(c) * 16 + (ph)] = clock64();                                                    \
   } while (0)
+__device__ unsigned long long g_trace1[16 * 8];
+__device__ unsigned long long g_cta[8192 * 5];  // start, end (globaltimer), smid, setup done, compute done
+#define TRACE1(ph)                                                                       \
+  do {                                                                                   \
+    if (blockIdx.x < 16 && threadIdx.x == 0) g_trace1[blockIdx.x * 8 + (ph)] = clock64(); \
+  } while (0)
 #else
+#define TRACE1(ph) \
+  do {             \
+  } while (0)
 #define TRACE(c, ph) \
   do {               \
   } while (0)
@@ -133,32 +142,37 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// acc (16 x 16, two m16n8 fragments) += X (16 x 16 block at x, stride kLd) * Y (16 x 16 at y).
+constexpr int kMsLd = 36;  // fp32 row stride of the solver scratch (32 columns + 4)
+
+// acc (16 x 16, two m16n8 fragments) += X (16 x 16 block at x, row stride
+// LX) * Y (16 x 16 at y, row stride LY).
+template <int LX = kLd, int LY = kLd>
 __device__ __forceinline__ void block_mma(float (&acc)[2][4], const float* x, const float* y, int lane) {
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int ks = 0; ks < 2; ++ks) {
     uint32_t af[4];
-    af[0] = __float_as_uint(x[g * kLd + ks * 8 + t]);
-    af[1] = __float_as_uint(x[(g + 8) * kLd + ks * 8 + t]);
-    af[2] = __float_as_uint(x[g * kLd + ks * 8 + t + 4]);
-    af[3] = __float_as_uint(x[(g + 8) * kLd + ks * 8 + t + 4]);
+    af[0] = __float_as_uint(x[g * LX + ks * 8 + t]);
+    af[1] = __float_as_uint(x[(g + 8) * LX + ks * 8 + t]);
+    af[2] = __float_as_uint(x[g * LX + ks * 8 + t + 4]);
+    af[3] = __float_as_uint(x[(g + 8) * LX + ks * 8 + t + 4]);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       uint32_t bf[2];
-      bf[0] = __float_as_uint(y[(ks * 8 + t) * kLd + nt * 8 + g]);
-      bf[1] = __float_as_uint(y[(ks * 8 + t + 4) * kLd + nt * 8 + g]);
+      bf[0] = __float_as_uint(y[(ks * 8 + t) * LY + nt * 8 + g]);
+      bf[1] = __float_as_uint(y[(ks * 8 + t + 4) * LY + nt * 8 + g]);
       mma_tf32(acc[nt], af, bf);
     }
   }
 }
 
+template <int LZ = kLd>
 __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], float sign, int lane) {
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
-    *reinterpret_cast<float2*>(z + g * kLd + nt * 8 + 2 * t) = make_float2(sign * acc[nt][0], sign * acc[nt][1]);
-    *reinterpret_cast<float2*>(z + (g + 8) * kLd + nt * 8 + 2 * t) =
+    *reinterpret_cast<float2*>(z + g * LZ + nt * 8 + 2 * t) = make_float2(sign * acc[nt][0], sign * acc[nt][1]);
+    *reinterpret_cast<float2*>(z + (g + 8) * LZ + nt * 8 + 2 * t) =
         make_float2(sign * acc[nt][2], sign * acc[nt][3]);
   }
 }
@@ -170,7 +184,7 @@ __device__ __forceinline__ void block_store(float* z, const float (&acc)[2][4], 
 // substitution (one warp each, one lane per column, fp32); T_10 = -D_1 A_10 D_0
 // and T_32 = -D_3 A_32 D_2; then the lower-left quadrant -T_bot A_bl T_top
 // through Y = A_bl T_top (TF32 warp MMAs).  Each block of A is last read
-// before the block of T that replaces it is written.  M is [32][kLd] scratch.
+// before the block of T that replaces it is written.  M is [32][kMsLd] scratch.
 __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int lane, int bar) {
   {
     const int bb = w * 16, c = lane & 15;
@@ -200,13 +214,13 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int
   tc::group_sync(bar, 128);
   if (w < 2) {  // T_10 (w 0) and T_32 (w 1)
     const int c = w * 2, r = c + 1;
-    float* X = M + w * 16 * kLd;
+    float* X = M + w * 16 * kMsLd;
     float acc[2][4] = {};
     block_mma(acc, AT + 16 * r * kLd + 16 * c, AT + 16 * c * kLd + 16 * c, lane);
-    block_store(X, acc, 1.f, lane);
+    block_store<kMsLd>(X, acc, 1.f, lane);
     __syncwarp();
     float acc2[2][4] = {};
-    block_mma(acc2, AT + 16 * r * kLd + 16 * r, X, lane);
+    block_mma<kLd, kMsLd>(acc2, AT + 16 * r * kLd + 16 * r, X, lane);
     block_store(AT + 16 * r * kLd + 16 * c, acc2, -1.f, lane);
   }
   tc::group_sync(bar, 128);
@@ -219,17 +233,17 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int
     } else {
       block_mma(acc, AT + 16 * r * kLd + 16, AT + 16 * kLd + 16, lane);         // A_r1 D_1
     }
-    block_store(M + (r - 2) * 16 * kLd + 16 * c, acc, 1.f, lane);
+    block_store<kMsLd>(M + (r - 2) * 16 * kMsLd + 16 * c, acc, 1.f, lane);
   }
   tc::group_sync(bar, 128);
   {
     const int r = 2 + (w >> 1), c = w & 1;
     float acc[2][4] = {};
     if (r == 2) {
-      block_mma(acc, AT + 32 * kLd + 32, M + 16 * c, lane);                     // D_2 Y_2c
+      block_mma<kLd, kMsLd>(acc, AT + 32 * kLd + 32, M + 16 * c, lane);         // D_2 Y_2c
     } else {
-      block_mma(acc, AT + 48 * kLd + 32, M + 16 * c, lane);                     // T_32 Y_2c
-      block_mma(acc, AT + 48 * kLd + 48, M + 16 * kLd + 16 * c, lane);          // D_3 Y_3c
+      block_mma<kLd, kMsLd>(acc, AT + 48 * kLd + 32, M + 16 * c, lane);         // T_32 Y_2c
+      block_mma<kLd, kMsLd>(acc, AT + 48 * kLd + 48, M + 16 * kMsLd + 16 * c, lane);  // D_3 Y_3c
     }
     block_store(AT + 16 * r * kLd + 16 * c, acc, -1.f, lane);
   }
@@ -241,24 +255,28 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int
 // head (pair index) h of the q/k head's group, so a GQA pair shares the
 // K K^T / Q K^T product.  Chunks run last-to-first so that the state kernel,
 // which starts at chunk 0, finds the most recent records still in L2.
+#ifndef GDN_K1_MINB
+#define GDN_K1_MINB 3
+#endif
 namespace intra {
 constexpr int kThreads = 256;
 constexpr uint32_t kKQ = 0;                      // [K | Q] per d_k block: 2 x 16 KB
 constexpr uint32_t kKQBlock = 16384;
 constexpr uint32_t kATHead = 64 * kLd * 4;       // 17408
 constexpr uint32_t kAT = 32768;                  // [2 heads] A -> T in place
-constexpr uint32_t kMsHead = 32 * kLd * 4;       // 8704: solver scratch per head, aliasing
+constexpr uint32_t kMsHead = 32 * kMsLd * 4;     // 4608: solver scratch per head, aliasing
                                                  // the K/Q tiles once the MMA is done
+constexpr uint32_t kPStage = 2 * kMsHead;        // [2 heads] P tile (8 KB), likewise
 constexpr uint32_t kVec = kAT + 2 * kATHead;     // [2 heads][G|beta|gamma|decay|Ee|Es][64]
 constexpr uint32_t kFlags = kVec + 2 * 6 * 64 * 4;
 constexpr uint32_t kBars = kFlags + 16;
 constexpr uint32_t kSmemBytes = kBars + 64;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
-static_assert(2 * kMsHead <= kAT, "solver scratch overflows the K/Q tiles");
+static_assert(kPStage + 2 * 8192 <= kAT, "solver scratch and P tiles overflow the K/Q tiles");
 }  // namespace intra
 
 template <bool BF16>
-__global__ void __launch_bounds__(intra::kThreads, 3)
+__global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
     intra_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
                  const __grid_constant__ CUtensorMap map_k) {
   using namespace intra;
@@ -269,6 +287,14 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);  // [0] TMA, [1] MMA
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2);
 
+#ifdef GDN_PREFILL_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 8192) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_cta[blockIdx.x * 5] = global_timer_ns();
+    g_cta[blockIdx.x * 5 + 2] = smid;
+  }
+#endif
   const gdn_prefill_args_t& a = p.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hh = warp >> 2, w4 = warp & 3, ht = tid & 127;
@@ -291,6 +317,10 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
   const uint32_t lane_base = static_cast<uint32_t>(w4 * 32) << 16;
   constexpr uint32_t kIdKQ = tc::idesc_f16(128, 64, false, false, BF16);
 
+  TRACE1(0);
+#ifdef GDN_PREFILL_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 8192) g_cta[blockIdx.x * 5 + 3] = global_timer_ns();
+#endif
   bool ok = true;
   if (tid == 0) {
     mbar_arrive_expect_tx(&bars[0], 4 * 8192);
@@ -319,6 +349,7 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
     if (lane == 0) mine = mbar_wait_bounded(&bars[1], 0);
     ok = !named_barrier_or(1, kThreads, !mine);
   }
+  TRACE1(1);
   if (!ok) {
     if (tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   } else {
@@ -337,6 +368,7 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
       const bool active = p0 + hh < p.group;  // an odd group leaves warps 4-7 idle
       const int h = hq * p.group + p0 + hh;
       unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
+      if (p0 > 0 && ht == 64) bulk_wait_read();  // the previous pair's P tile has left
       if (active && ht < kC) {
         const int t = t0 + ht;
         float gv = 0.f, bv = 0.f;  // padded tokens: no decay, no update
@@ -381,6 +413,7 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
         reinterpret_cast<float2*>(rec + kWsVec + 256)[lane] = dec;
       }
       tc::group_sync(bar, 128);
+      TRACE1(2);
       if (active) {  // A rows (TMEM lanes 0-63, warps 0-1) and P rows (lanes 64-127, warps 2-3)
         // exp(G_i - G_j) for j <= i, factored by 16-token blocks I = i/16, J = j/16:
         //   J < I : exp(G_i - G_end(J)) exp(G_end(J) - G_j)     (both factors <= 1)
@@ -428,39 +461,67 @@ __global__ void __launch_bounds__(intra::kThreads, 3)
               *reinterpret_cast<float4*>(AT + i * kLd + cb * 32 + j4) =
                   make_float4(r[j4], r[j4 + 1], r[j4 + 2], r[j4 + 3]);
           } else {
-            store_row16_global<BF16>(rec + kWsP, i, cb * 4, r);
-            store_row16_global<BF16>(rec + kWsP, i, cb * 4 + 2, r + 16);
+            const uint32_t pst = sb + kKQ + kPStage + hh * 8192;
+            store_row16<BF16>(pst, i, cb * 4, r);
+            store_row16<BF16>(pst, i, cb * 4 + 2, r + 16);
           }
         }
+        if (w4 >= 2) tc::fence_proxy_async();  // the P tile is read by a bulk copy
       }
       tc::group_sync(bar, 128);
+      if (active && ht == 64) {  // the whole P tile to its record in one bulk copy
+        bulk_s2g(rec + kWsP, smem + kKQ + kPStage + hh * 8192, 8192);
+        bulk_commit();
+      }
+      TRACE1(3);
       if (active) solve_unit_lower(AT, Ms, w4, lane, bar);
-      if (active) {  // T_w = T diag(beta gamma), T_u = T diag(beta); thread: row i, 32 columns
-        const int i = ht >> 1, jh = ht & 1;
-        float tw[32], tu[32];
+      TRACE1(4);
+      if (active) {
+        // T_w = T diag(beta gamma), T_u = T diag(beta).  Warp w4 writes rows
+        // 16 w4 .. 16 w4 + 15; lane l the 16-byte chunk l % 8 (columns
+        // 8 (l % 8) ..) of rows 16 w4 + l / 8 + 4 s, so each store instruction
+        // covers four whole 128-byte rows (512 contiguous bytes).
+        const int ch = lane & 7;
+        const float4 b0 = *reinterpret_cast<const float4*>(sBeta + 8 * ch);
+        const float4 b1 = *reinterpret_cast<const float4*>(sBeta + 8 * ch + 4);
+        const float4 g0 = *reinterpret_cast<const float4*>(sGam + 8 * ch);
+        const float4 g1 = *reinterpret_cast<const float4*>(sGam + 8 * ch + 4);
+        const float bj[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const float gj[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-        for (int j4 = 0; j4 < 32; j4 += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(AT + i * kLd + jh * 32 + j4);
-          const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+        for (int s4 = 0; s4 < 4; ++s4) {
+          const int i = 16 * w4 + (lane >> 3) + 4 * s4;
+          const float4 t0 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * ch);
+          const float4 t1 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * ch + 4);
+          const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+          uint32_t uw[4], uu[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = jh * 32 + j4 + e;
-            const float t = (j <= i) ? tv[e] : 0.f;
-            tu[j4 + e] = t * sBeta[j];
-            tw[j4 + e] = tu[j4 + e] * sGam[j];
+            const int j0 = 8 * ch + 2 * e;
+            const float tu0 = (j0 <= i) ? tv[2 * e] * bj[2 * e] : 0.f;
+            const float tu1 = (j0 + 1 <= i) ? tv[2 * e + 1] * bj[2 * e + 1] : 0.f;
+            uu[e] = tc::pack2<BF16>(tu0, tu1);
+            uw[e] = tc::pack2<BF16>(tu0 * gj[2 * e], tu1 * gj[2 * e + 1]);
           }
+          const uint32_t off = tc::sw128_offset(i, ch);
+          *reinterpret_cast<uint4*>(rec + kWsTw + off) = make_uint4(uw[0], uw[1], uw[2], uw[3]);
+          *reinterpret_cast<uint4*>(rec + kWsTu + off) = make_uint4(uu[0], uu[1], uu[2], uu[3]);
         }
-        store_row16_global<BF16>(rec + kWsTw, i, jh * 4, tw);
-        store_row16_global<BF16>(rec + kWsTw, i, jh * 4 + 2, tw + 16);
-        store_row16_global<BF16>(rec + kWsTu, i, jh * 4, tu);
-        store_row16_global<BF16>(rec + kWsTu, i, jh * 4 + 2, tu + 16);
       }
       tc::group_sync(bar, 128);  // AT and the vectors are reused by the next pair
+      TRACE1(5);
     }
   }
+#ifdef GDN_PREFILL_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 8192) g_cta[blockIdx.x * 5 + 4] = global_timer_ns();
+#endif
+  if (ht == 64) bulk_wait_all();  // the P tiles have left shared memory
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 64);
+#ifdef GDN_PREFILL_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 8192) g_cta[blockIdx.x * 5 + 1] = global_timer_ns();
+#endif
 }
 
 // ============================================================ state kernel
@@ -966,6 +1027,15 @@ int validate(const gdn_prefill_args_t* a) {
 }  // namespace gdn
 
 #ifdef GDN_PREFILL_TRACE
+extern "C" int gdn_prefill_cta_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, gdn::prefill::g_cta, sizeof(gdn::prefill::g_cta)) == cudaSuccess ? 0 : 1;
+}
+extern "C" int gdn_prefill_trace1_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, gdn::prefill::g_trace1, sizeof(gdn::prefill::g_trace1)) ==
+                 cudaSuccess
+             ? 0
+             : 1;
+}
 extern "C" int gdn_prefill_trace_read(unsigned long long* host) {
   return cudaMemcpyFromSymbol(host, gdn::prefill::g_trace, sizeof(gdn::prefill::g_trace)) ==
                  cudaSuccess

@@ -106,6 +106,27 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Shared -> global 1-D bulk copy in the thread's bulk async-group (no
+// multicast).  src, dst 16-byte aligned; bytes a multiple of 16.  The source
+// must have been made visible to the async proxy (fence.proxy.async).
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until every committed bulk async-group of this thread has finished
+// reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until every committed bulk async-group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // 2-D tiled TMA load (no multicast) of the box at (x = column, y = row) of
 // `map` into shared memory, completing on an mbarrier.  x * element size must
 // be a multiple of 16 bytes.
