@@ -304,6 +304,20 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
   const int b = bq / a.Hqk, hq = bq % a.Hqk;
   const int T = a.T, t0 = c * kC;
 
+  // raw gate and beta of token ht of value head (pair slot) hh, pair p0;
+  // issued before anything else so that their latency overlaps the set-up
+  auto load_gate = [&](int p0, float& gv, float& bv) {
+    gv = 0.f;  // padded tokens: no decay, no update
+    bv = 0.f;
+    const int t = t0 + ht;
+    if (p0 + hh < p.group && ht < kC && t < T) {
+      const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + hq * p.group + p0 + hh;
+      gv = load_any(a.g, gi, a.g_dtype);
+      bv = load_any(a.beta, gi, a.beta_dtype);
+    }
+  };
+  float gv0, bv0;
+  load_gate(0, gv0, bv0);
   if (warp == 0) tc::tmem_alloc(tmem_holder, 64);
   if (tid == 0) {
     mbar_init(&bars[0], 1);
@@ -317,19 +331,76 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
   const uint32_t lane_base = static_cast<uint32_t>(w4 * 32) << 16;
   constexpr uint32_t kIdKQ = tc::idesc_f16(128, 64, false, false, BF16);
 
+  const int bar = 2 + hh;
+  float* AT = reinterpret_cast<float*>(smem + kAT + hh * kATHead);
+  float* Ms = reinterpret_cast<float*>(smem + kKQ + hh * kMsHead);
+  float* sG = reinterpret_cast<float*>(smem + kVec) + hh * 384;
+  float* sBeta = sG + 64;
+  float* sGam = sG + 128;
+  float* sDec = sG + 192;
+  float* sEe = sG + 256;   // exp(G_end(J) - G_j)
+  float* sEs = sG + 320;   // exp(G_start(J) - G_j)
+  int* sFast = reinterpret_cast<int*>(smem + kFlags) + hh;
+  // The in-chunk cumulative log gate of value head (pair slot) hh of pair p0
+  // and the exponentials derived from it (independent of the K/Q tiles).
+  auto gates = [&](int p0, float gv, float bv) {
+    const bool active = p0 + hh < p.group;
+    const int h = hq * p.group + p0 + hh;
+    unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
+    if (active && ht < kC) {
+      sG[ht] = gv;
+      sBeta[ht] = bv;
+    }
+    tc::group_sync(bar, 128);
+    if (active && w4 == 0) {  // in-chunk cumulative log gate; lane l owns tokens 2l, 2l+1
+      const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
+      float run = g0 + g1;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float o = __shfl_up_sync(0xffffffffu, run, off);
+        if (lane >= off) run += o;
+      }
+      const float excl = run - (g0 + g1);
+      const float GC = __shfl_sync(0xffffffffu, run, 31);
+      const float Ga = excl + g0, Gb = run;
+      // G at the first and last token of this lane's 16-token block
+      const float Gs = __shfl_sync(0xffffffffu, Ga, lane & ~7);
+      const float Ge = __shfl_sync(0xffffffffu, Gb, lane | 7);
+      // the factored exponentials below stay finite when no block decays by
+      // more than 80 (nats) within itself; otherwise the direct form is used
+      const bool fast = __all_sync(0xffffffffu, Gs - Ge <= 80.f);
+      __syncwarp();
+      sG[2 * lane] = Ga;
+      sG[2 * lane + 1] = Gb;
+      const float2 gam = make_float2(__expf(Ga), __expf(Gb));
+      const float2 dec = make_float2(__expf(GC - Ga), __expf(GC - Gb));  // V'' row scale
+      reinterpret_cast<float2*>(sGam)[lane] = gam;
+      reinterpret_cast<float2*>(sDec)[lane] = dec;
+      reinterpret_cast<float2*>(sEe)[lane] = make_float2(__expf(Ge - Ga), __expf(Ge - Gb));
+      reinterpret_cast<float2*>(sEs)[lane] =
+          make_float2(__expf(fminf(Gs - Ga, 80.f)), __expf(fminf(Gs - Gb, 80.f)));
+      if (lane == 0) *sFast = fast ? 1 : 0;
+      reinterpret_cast<float2*>(rec + kWsVec)[lane] = gam;
+      reinterpret_cast<float2*>(rec + kWsVec + 256)[lane] = dec;
+    }
+    tc::group_sync(bar, 128);
+  };
   TRACE1(0);
 #ifdef GDN_PREFILL_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 8192) g_cta[blockIdx.x * 5 + 3] = global_timer_ns();
 #endif
-  bool ok = true;
   if (tid == 0) {
     mbar_arrive_expect_tx(&bars[0], 4 * 8192);
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
-      unsigned char* kq = smem + kKQ + blk * kKQBlock;
-      tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
-      tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
+    unsigned char* kq = smem + kKQ + blk * kKQBlock;
+    tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
+    tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
     }
+  }
+  gates(0, gv0, bv0);  // while the K/Q tiles are in flight
+  bool ok = true;
+  if (tid == 0) {
     // [K;Q] K^T: TMEM lanes 0-63 hold K K^T rows, lanes 64-127 Q K^T rows
     ok = mbar_wait_bounded(&bars[0], 0);
     if (ok) {
@@ -354,65 +425,16 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
     if (tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   } else {
     tc::fence_after_sync();
-    const int bar = 2 + hh;
-    float* AT = reinterpret_cast<float*>(smem + kAT + hh * kATHead);
-    float* Ms = reinterpret_cast<float*>(smem + kKQ + hh * kMsHead);
-    float* sG = reinterpret_cast<float*>(smem + kVec) + hh * 384;
-    float* sBeta = sG + 64;
-    float* sGam = sG + 128;
-    float* sDec = sG + 192;
-    float* sEe = sG + 256;   // exp(G_end(J) - G_j)
-    float* sEs = sG + 320;   // exp(G_start(J) - G_j)
-    int* sFast = reinterpret_cast<int*>(smem + kFlags) + hh;
     for (int p0 = 0; p0 < p.group; p0 += 2) {
       const bool active = p0 + hh < p.group;  // an odd group leaves warps 4-7 idle
       const int h = hq * p.group + p0 + hh;
       unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
-      if (p0 > 0 && ht == 64) bulk_wait_read();  // the previous pair's P tile has left
-      if (active && ht < kC) {
-        const int t = t0 + ht;
-        float gv = 0.f, bv = 0.f;  // padded tokens: no decay, no update
-        if (t < T) {
-          const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + h;
-          gv = load_any(a.g, gi, a.g_dtype);
-          bv = load_any(a.beta, gi, a.beta_dtype);
-        }
-        sG[ht] = gv;
-        sBeta[ht] = bv;
+      if (p0 > 0) {
+        if (ht == 64) bulk_wait_read();  // the previous pair's P tile has left
+        float gv, bv;
+        load_gate(p0, gv, bv);
+        gates(p0, gv, bv);
       }
-      tc::group_sync(bar, 128);
-      if (active && w4 == 0) {  // in-chunk cumulative log gate; lane l owns tokens 2l, 2l+1
-        const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
-        float run = g0 + g1;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float o = __shfl_up_sync(0xffffffffu, run, off);
-          if (lane >= off) run += o;
-        }
-        const float excl = run - (g0 + g1);
-        const float GC = __shfl_sync(0xffffffffu, run, 31);
-        const float Ga = excl + g0, Gb = run;
-        // G at the first and last token of this lane's 16-token block
-        const float Gs = __shfl_sync(0xffffffffu, Ga, lane & ~7);
-        const float Ge = __shfl_sync(0xffffffffu, Gb, lane | 7);
-        // the factored exponentials below stay finite when no block decays by
-        // more than 80 (nats) within itself; otherwise the direct form is used
-        const bool fast = __all_sync(0xffffffffu, Gs - Ge <= 80.f);
-        __syncwarp();
-        sG[2 * lane] = Ga;
-        sG[2 * lane + 1] = Gb;
-        const float2 gam = make_float2(__expf(Ga), __expf(Gb));
-        const float2 dec = make_float2(__expf(GC - Ga), __expf(GC - Gb));  // V'' row scale
-        reinterpret_cast<float2*>(sGam)[lane] = gam;
-        reinterpret_cast<float2*>(sDec)[lane] = dec;
-        reinterpret_cast<float2*>(sEe)[lane] = make_float2(__expf(Ge - Ga), __expf(Ge - Gb));
-        reinterpret_cast<float2*>(sEs)[lane] =
-            make_float2(__expf(fminf(Gs - Ga, 80.f)), __expf(fminf(Gs - Gb, 80.f)));
-        if (lane == 0) *sFast = fast ? 1 : 0;
-        reinterpret_cast<float2*>(rec + kWsVec)[lane] = gam;
-        reinterpret_cast<float2*>(rec + kWsVec + 256)[lane] = dec;
-      }
-      tc::group_sync(bar, 128);
       TRACE1(2);
       if (active) {  // A rows (TMEM lanes 0-63, warps 0-1) and P rows (lanes 64-127, warps 2-3)
         // exp(G_i - G_j) for j <= i, factored by 16-token blocks I = i/16, J = j/16:
