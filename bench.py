@@ -226,19 +226,29 @@ def run_gpu(args, world, rank, local):
     # decode of step i + 1; step i + 2 waits for it before reusing the buffer
     outs = [torch.empty((B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     out = outs[0]
-    gmode = args.gather if args.gather != "auto" else ("ce" if world <= 4 else "nccl")
+    gmode = args.gather if args.gather != "auto" else "fused"
     ce = world > 1 and gmode == "ce"
+    fused = world > 1 and gmode == "fused"
     res = args.sm_reserve if args.sm_reserve >= 0 else min(48, 8 * world if world > 2 else 16)
-    res = res if (world > 1 and not ce) else 0
-    steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
-    steps2 = [pkg.DecodeStep(*t, state, out=outs[1], sm_reserve=res) for t in toks]
+    res = res if (world > 1 and gmode == "nccl") else 0
+    if fused:
+        # the decode kernel writes every output row into every rank's
+        # head-major buffer itself (NVLink stores) and signals arrival
+        fg = sharded.FusedGather(B, HV, D, shard.h0, hv, torch.bfloat16, dev)
+        fsteps = [[fg.decode_step(slot, *t, state) for slot in range(2)] for t in toks]
+    else:
+        steps = [pkg.DecodeStep(*t, state, out=outs[0], sm_reserve=res) for t in toks]
+        steps2 = [pkg.DecodeStep(*t, state, out=outs[1], sm_reserve=res) for t in toks]
     gbufs = [torch.empty((world, B, hv, D), dtype=torch.bfloat16, device=dev) for _ in range(2)] \
         if world > 1 else None
     gather_buf = gbufs[0] if world > 1 else None
     works = [None, None]
 
     def launch(i):
-        (steps if i % 2 == 0 else steps2)[i % pool]()
+        if fused:
+            fg.launch(fsteps[i % pool])
+        else:
+            (steps if i % 2 == 0 else steps2)[i % pool]()
 
     if ce:
         # copy-engine all-gather (no SMs): push on a side stream after each
@@ -252,6 +262,8 @@ def run_gpu(args, world, rank, local):
         gstep = [0]
 
     def gather(i):
+        if fused:
+            return  # done inside the decode kernel
         if world > 1 and ce:
             gstep[0] += 1
             ms_ = torch.cuda.current_stream(dev)
@@ -300,7 +312,7 @@ def run_gpu(args, world, rank, local):
     settle(args.warmup + 1)
     join()
     pkg.check_device_status(dev)
-    use_graph = world > 1 and not args.no_graph and not ce
+    use_graph = world > 1 and not args.no_graph and gmode == "nccl"
     n_kev = min(args.steps, 200) if use_graph else args.steps
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_kev)]
@@ -370,11 +382,14 @@ def run_gpu(args, world, rank, local):
 
     # ---- parity of one more step (and of its gather) against the C oracle
     def gathered(i):  # [N, B, hv, d] rank-major slot holding step i's gathered outputs
+        if fused:
+            return fg.wait(fg.step).view(B, world, hv, D).permute(1, 0, 2, 3)
         if ce:
             return pg.buf[gstep[0] % 2].view(world, B, hv, D)
         return gbufs[i % 2]
 
-    parity = decode_parity(graft.oracle(), toks, state, outs, launch, gather, settle, join,
+    last_out = (lambda: fg.local_out(fg.step % 2)) if fused else (lambda: outs[0])
+    parity = decode_parity(graft.oracle(), toks, state, last_out, launch, gather, settle, join,
                            gathered, shard, world, rank, dev)
 
     # ---- e2e through the public API with pinned host buffers
@@ -406,8 +421,9 @@ def run_gpu(args, world, rank, local):
                    "global_batch": B, "Hqk": HQK, "Hv": HV, "d_k": D, "d_v": D,
                    "io_dtype": "bf16", "state": "fp32 in place",
                    "parallelism": f"value-head shard x{world}" + (
-                       (" + copy-engine all-gather of o" if ce else " + NCCL all-gather of o")
-                                                                 if world > 1 else ""),
+                       {"ce": " + copy-engine all-gather of o", "nccl": " + NCCL all-gather of o",
+                        "fused": " + all-gather of o fused into the decode kernel (NVLink stores)"}[gmode]
+                       if world > 1 else ""),
                    "l2": "inputs larger than L2 (4.3 GB state), no flush"},
         "tokens_per_s": round(B / (ms * 1e-3), 1),
         "pct_of_8TBs_per_gpu": round(100 * value / world / 8000.0, 2),
@@ -425,7 +441,9 @@ def run_gpu(args, world, rank, local):
         "gpu_launches": timed_steps,
         "cuda_graph": graph is not None,
         "allgather_overlapped": world > 1 and not args.no_overlap,
-        "allgather": ("copy-engine push over NVLink (IPC)" if ce else "NCCL") if world > 1 else None,
+        "allgather": {"ce": "copy-engine push over NVLink (IPC)", "nccl": "NCCL",
+                      "fused": "decode kernel stores into every rank's buffer over NVLink (IPC)"}[gmode]
+                     if world > 1 else None,
         "sm_reserve": res,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
@@ -434,7 +452,7 @@ def run_gpu(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
-def decode_parity(orc, toks, state, outs, launch, gather, settle, join, gathered, shard,
+def decode_parity(orc, toks, state, last_out, launch, gather, settle, join, gathered, shard,
                   world, rank, dev, n_seq=8):
     """One more decode step after the timed region, through the same launch
     and gather path as the timed steps, checked against the C oracle (the
@@ -449,12 +467,12 @@ def decode_parity(orc, toks, state, outs, launch, gather, settle, join, gathered
     idx = torch.linspace(0, B - 1, n_seq).round().long().to(dev)
     q, k, v, g, beta = [t.index_select(0, idx).float().cpu() for t in toks[0]]
     S0 = state.index_select(0, idx).cpu().numpy()
-    launch(0)          # bound to toks[0] and outs[0]
+    launch(0)          # bound to toks[0]
     gather(0)
     settle(0)
     join()
     torch.cuda.synchronize(dev)
-    o_dev = outs[0].index_select(0, idx).float().cpu().numpy()
+    o_dev = last_out().index_select(0, idx).float().cpu().numpy()
     S1 = state.index_select(0, idx).cpu().numpy()
     o_ref, s_ref = orc.gdn_decode_steps(q[None], k[None], v[None], g[None], beta[None], S0)
     o_ref = o_ref[0]
@@ -893,9 +911,9 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the decode leaves to the overlapped all-gather (N>1); default "
                          "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
-    ap.add_argument("--gather", default="auto", choices=("auto", "ce", "nccl"),
-                    help="N>1 output all-gather: copy engines over NVLink (ce) or NCCL; auto "
-                         "picks the measured faster one (ce at N<=4, NCCL + SM reservation at N=8)")
+    ap.add_argument("--gather", default="auto", choices=("auto", "fused", "ce", "nccl"),
+                    help="N>1 output all-gather: fused into the decode kernel (NVLink stores, the "
+                         "default), copy engines over NVLink (ce) or NCCL")
     ap.add_argument("--no-graph", action="store_true",
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",

@@ -25,6 +25,7 @@ DEVERR_BITS = {
     1 << 1: "producer timed out waiting for a free ring slot",
     1 << 2: "tensor-core completion was never signalled",
     1 << 3: "copies in flight never landed while aborting",
+    1 << 4: "a peer rank never released a gathered-output slot",
 }
 
 # Every function the header declares (checked by the CPU test suite).
@@ -44,6 +45,7 @@ EXPORTED = (
     "gdn_ipc_close",
     "gdn_gather_push",
     "gdn_gather_wait",
+    "gdn_gather_wait_counter",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -54,6 +56,19 @@ class GDNError(RuntimeError):
     def __init__(self, msg: str, code: int = -1):
         super().__init__(msg)
         self.code = code
+
+
+class PeerOut(ctypes.Structure):
+    _fields_ = [
+        ("o_peer", ctypes.c_void_p * 7),
+        ("arrive", ctypes.c_void_p * 8),
+        ("free_flags", ctypes.c_void_p * 8),
+        ("cta_done", ctypes.c_void_p),
+        ("n_ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("step", ctypes.c_uint32),
+        ("reserved", ctypes.c_int32),
+    ]
 
 
 class DecodeArgs(ctypes.Structure):
@@ -83,6 +98,7 @@ class DecodeArgs(ctypes.Structure):
         ("z_sb", ctypes.c_int64), ("z_sh", ctypes.c_int64),
         ("norm_weight", ctypes.c_void_p),
         ("norm_eps", ctypes.c_float),
+        ("peer_out", ctypes.c_void_p),
     ]
 
 
@@ -147,6 +163,8 @@ def load(path: str | Path | None = None):
         L.gdn_gather_push.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp), ctypes.POINTER(vp),
                                       i32, ctypes.c_uint32, vp]
         L.gdn_gather_wait.argtypes = [vp, i32, ctypes.c_uint32, vp]
+        L.gdn_gather_wait_counter.argtypes = [vp, ctypes.c_uint32, vp, vp]
+        L.gdn_gather_wait_counter.restype = ctypes.c_int
         for fn in (L.gdn_ipc_handle, L.gdn_ipc_open, L.gdn_ipc_close, L.gdn_gather_push,
                    L.gdn_gather_wait):
             fn.restype = ctypes.c_int

@@ -160,7 +160,8 @@ class DecodeStep:
 
     def __init__(self, q, k, v, g, beta, state, *, out=None, state_out=None, scale=1.0,
                  gate="log", kda=False, sm_reserve=0, l2norm_qk=False, l2_eps=1e-6,
-                 A_log=None, dt_bias=None, z=None, norm_weight=None, norm_eps=1e-6):
+                 A_log=None, dt_bias=None, z=None, norm_weight=None, norm_eps=1e-6,
+                 peer_out=None):
         dev = _require_cuda(q, k, v, g, beta, state)
         self.out = out if out is not None else torch.empty(
             (v.shape[0], v.shape[1], v.shape[2]), dtype=q.dtype, device=dev)
@@ -170,6 +171,9 @@ class DecodeStep:
         self._args = _decode_args(q, k, v, g, beta, state, state_out, self.out, scale, gate, kda,
                                   sm_reserve, l2norm_qk, l2_eps, A_log, dt_bias, z, norm_weight,
                                   norm_eps)
+        if peer_out is not None:  # a _lib.PeerOut owned by sharded.FusedGather
+            self._peer = peer_out
+            self._args.peer_out = ctypes.addressof(peer_out)
         self._argp = ctypes.byref(self._args)
         L = _lib.load()
         self._fn = L.kda_decode_launch if kda else L.gdn_decode_launch

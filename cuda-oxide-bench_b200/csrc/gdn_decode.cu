@@ -50,7 +50,31 @@ struct DecodeParams {
   int32_t stage_bytes;
   int32_t contiguous; // BV == d_v: a slab is one contiguous block
   int32_t g_row_bytes;
+  int32_t has_peer;   // fused output all-gather (a.peer_out) in use
+  gdn_peer_out_t po;  // its pointers, by value
 };
+
+// Acquire load of a flag another GPU writes (system scope).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait (kWaitLimitNs) until every rank has released the output slot
+// this step overwrites: free[j] >= step - 2 for all ranks j.
+__device__ __forceinline__ bool peer_slots_free(const gdn_peer_out_t& po) {
+  if (po.step < 3) return true;
+  const uint32_t need = po.step - 2;
+  const uint32_t* fr = po.free_flags[po.rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int j = 0; j < po.n_ranks; ++j) {
+    while (ld_acquire_sys(fr + j) < need) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+  return true;
+}
 
 // SB: bytes per state element (4 = fp32, the default; 2 = the optional fp16
 // state, which halves the bytes a step streams).
@@ -187,6 +211,14 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
   const int cg = tid % Tr::kColGroups;         // float4 column group
   const int rg = tid / Tr::kColGroups;         // first row of this thread
   const float scale = a.scale;
+  // fused all-gather: this rank has consumed step - 1 (its reads of gathered
+  // outputs precede this launch), so tell every rank
+  if (p.has_peer && blockIdx.x == 0 && tid == 0) {
+    for (int j = 0; j < p.po.n_ranks; ++j)
+      atomicMax_system(p.po.free_flags[j] + p.po.rank, p.po.step - 1);
+  }
+  bool peer_ok = p.has_peer != 0;  // peer stores allowed (slot released)
+  bool peer_checked = false;
   int it = 0;
   for (int64_t slab = blockIdx.x; slab < p.total_slabs; slab += gridDim.x, ++it) {
     const int stage = it % p.stages;
@@ -366,9 +398,23 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
       IO ov[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) ov[e] = from_f32<IO>(of[e]);
-      IO* o = static_cast<IO*>(a.o) + b * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
-              static_cast<int64_t>(vb) * BV + cg * 4;
+      const int64_t off = b * a.o_sb + static_cast<int64_t>(h) * a.o_sh + static_cast<int64_t>(vb) * BV + cg * 4;
+      IO* o = static_cast<IO*>(a.o) + off;
       *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(ov);
+      if (peer_ok) {
+        if (!peer_checked) {
+          peer_checked = true;
+          if (!peer_slots_free(p.po)) {
+            peer_ok = false;
+            report(a.status, GDN_DEVERR_PEER_TIMEOUT);
+          }
+        }
+        if (peer_ok) {
+          for (int i = 0; i < p.po.n_ranks - 1; ++i)
+            *reinterpret_cast<uint2*>(static_cast<IO*>(p.po.o_peer[i]) + off) =
+                *reinterpret_cast<const uint2*>(ov);
+        }
+      }
     }
 
     unsigned char* dst = reinterpret_cast<unsigned char*>(a.state_out) +
@@ -389,6 +435,20 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
                      "r"(*reinterpret_cast<const uint32_t*>(&lo)),
                      "r"(*reinterpret_cast<const uint32_t*>(&hi))
                      : "memory");
+      }
+    }
+  }
+  if (p.has_peer) {
+    // every output store of this CTA (local and remote) is made visible at
+    // system scope before the CTA counts itself done; the last CTA of the
+    // grid then adds 1 to every rank's arrival counter
+    __threadfence_system();
+    const bool aborted = named_barrier_or(1, Tr::kConsumers, *abort_flag != 0);
+    if (tid == 0 && !aborted) {
+      const uint32_t old = atomicAdd(p.po.cta_done, 1u);
+      if (old + 1u == p.po.step * gridDim.x) {
+        __threadfence_system();
+        for (int j = 0; j < p.po.n_ranks; ++j) atomicAdd_system(p.po.arrive[j], 1u);
       }
     }
   }
@@ -423,6 +483,9 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   p.stage_bytes = Tr::kStageBytes;
   p.contiguous = (BV == a.dv) ? 1 : 0;
   p.g_row_bytes = KDA ? DK * host_dtype_size(a.g_dtype) : 0;
+  p.has_peer = a.peer_out ? 1 : 0;
+  if (a.peer_out) p.po = *a.peer_out;
+  else std::memset(&p.po, 0, sizeof(p.po));
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
   if (!p.contiguous) {
@@ -459,6 +522,16 @@ static int validate_decode(const gdn_decode_args_t* a, bool kda) {
     if (!aligned16(a->z) || !stride_ok(a->z_sb, 2) || !stride_ok(a->z_sh, 2)) return GDN_ERR_ALIGN;
   }
   if (a->state_dtype != GDN_DT_F32 && a->state_dtype != GDN_DT_F16) return GDN_ERR_DTYPE;
+  if (a->peer_out) {
+    const gdn_peer_out_t& po = *a->peer_out;
+    if (po.n_ranks < 2 || po.n_ranks > 8 || po.rank < 0 || po.rank >= po.n_ranks || po.step < 1)
+      return GDN_ERR_SHAPE;
+    if (!po.cta_done) return GDN_ERR_NULL;
+    for (int j = 0; j < po.n_ranks; ++j)
+      if (!po.arrive[j] || !po.free_flags[j]) return GDN_ERR_NULL;
+    for (int i = 0; i < po.n_ranks - 1; ++i)
+      if (!po.o_peer[i] || !aligned16(po.o_peer[i])) return GDN_ERR_NULL;
+  }
   if (a->flags & GDN_DECODE_GATE_RAW) {
     if (kda) return GDN_ERR_DTYPE;  // the raw-gate formula is the scalar GDN gate
     if (!a->A_log || !a->dt_bias) return GDN_ERR_NULL;

@@ -122,3 +122,34 @@ extern "C" int gdn_gather_wait(const uint32_t* flags, int32_t n, uint32_t value,
       return GDN_ERR_LAUNCH;
   return GDN_OK;
 }
+
+// ------------------------------------------------------------------------
+// Consumer side of the fused output all-gather of the decode kernel
+// (gdn_peer_out_t): one thread waits, bounded, until an arrival counter that
+// peer GPUs increment reaches `target`.  Stream-ordered after this rank's own
+// decode, so later work on the stream sees every rank's outputs.
+#include "ptx.cuh"
+
+namespace {
+
+__global__ void counter_wait_kernel(const uint32_t* counter, uint32_t target, uint32_t* status) {
+  const uint64_t t0 = gdn::global_timer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    if (static_cast<int32_t>(v - target) >= 0) return;  // v >= target, modulo 2^32
+    if (gdn::global_timer_ns() - t0 > gdn::kWaitLimitNs) {
+      gdn::report(status, GDN_DEVERR_PEER_TIMEOUT);
+      return;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int gdn_gather_wait_counter(const uint32_t* counter, uint32_t target, uint32_t* status,
+                                       gdn_stream_t stream) {
+  if (!counter) return GDN_ERR_NULL;
+  counter_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(counter, target, status);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}

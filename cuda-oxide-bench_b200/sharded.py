@@ -226,6 +226,102 @@ class PeerGather:
         self._opened = []
 
 
+class FusedGather:
+    """Output all-gather fused into the decode kernel (gdn_peer_out_t).
+
+    Every rank holds two full output buffers ``out[slot]`` [B, Hv, d_v]
+    (head-major: the gathered result needs no permute), an arrival counter,
+    a finished-CTA counter and ``free[N]`` flags, in one allocation exported
+    through CUDA IPC.  ``decode_step(...)`` binds a :class:`DecodeStep` whose
+    kernel writes this rank's heads of step s into slot ``s % 2`` of every
+    rank's buffer with plain NVLink stores and signals arrival itself; no copy
+    engine, collective or host synchronisation runs per step.
+
+    Use: ``launch(steps)`` runs the next step (``steps`` = the two bound
+    DecodeSteps, one per slot) and returns its step number; ``wait(step)``
+    makes the current stream wait (bounded, on the GPU) until every rank's
+    outputs of that step are in ``out[step % 2]``.  Reads of a step's
+    outputs must be stream-ordered before this rank's next ``launch``.
+    Every rank must launch the same sequence of steps.
+    """
+
+    def __init__(self, B: int, Hv: int, dv: int, h0: int, hv: int, dtype, device, group=None):
+        from . import _lib
+        self._lib = _lib.load()
+        self._L = _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("the fused gather spans 2..8 ranks")
+        self.device = torch.device(device)
+        self.B, self.Hv, self.dv, self.h0, self.hv = B, Hv, dv, h0, hv
+        esz = torch.empty((), dtype=dtype).element_size()
+        slot_bytes = B * Hv * dv * esz
+        flag_off = (2 * slot_bytes + 255) // 256 * 256
+        n = self.world
+        self.raw = torch.zeros(flag_off + 8 + 4 * n, dtype=torch.uint8, device=self.device)
+        self.out = [self.raw[s * slot_bytes:(s + 1) * slot_bytes].view(dtype).view(B, Hv, dv)
+                    for s in range(2)]
+        flags = self.raw[flag_off:].view(torch.int32)
+        self.arrive = flags[0:1]
+        h = PeerGather._handle(self, self.raw)
+        allh = [None] * n
+        dist.all_gather_object(allh, h, group=group)
+        self._opened = []
+        bases = [self.raw.data_ptr() if p == self.rank else PeerGather._open(self, hp)
+                 for p, hp in enumerate(allh)]
+        head_off = h0 * dv * esz
+        self._po = []
+        for slot in range(2):
+            po = _lib.PeerOut()
+            peers = [bases[p] + slot * slot_bytes + head_off for p in range(n) if p != self.rank]
+            for i, ptr in enumerate(peers):
+                po.o_peer[i] = ptr
+            for p in range(n):
+                po.arrive[p] = bases[p] + flag_off
+                po.free_flags[p] = bases[p] + flag_off + 8
+            po.cta_done = bases[self.rank] + flag_off + 4
+            po.n_ranks, po.rank, po.step = n, self.rank, 1
+            self._po.append(po)
+        self.step = 0
+        self.group = group
+        dist.barrier(group=group)
+
+    def local_out(self, slot: int) -> torch.Tensor:
+        """This rank's heads inside its own buffer of ``slot`` (the ``out``
+        a DecodeStep writes)."""
+        return self.out[slot][:, self.h0:self.h0 + self.hv]
+
+    def decode_step(self, slot: int, q, k, v, g, beta, state, **kw):
+        from .api import DecodeStep
+        return DecodeStep(q, k, v, g, beta, state, out=self.local_out(slot),
+                          peer_out=self._po[slot], **kw)
+
+    def launch(self, steps) -> int:
+        """Runs the next decode step through ``steps[slot]`` and returns its
+        1-based step number."""
+        self.step += 1
+        slot = self.step % 2
+        self._po[slot].step = self.step
+        steps[slot]()
+        return self.step
+
+    def wait(self, step: int, stream=None) -> torch.Tensor:
+        """Stream-waits until every rank's outputs of ``step`` have arrived;
+        returns the gathered [B, Hv, d_v] buffer of that step."""
+        from .api import status_word
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        self._L.check(self._lib.gdn_gather_wait_counter(
+            self.arrive.data_ptr(), (step * self.world) & 0xFFFFFFFF,
+            status_word(self.device).data_ptr(), s), "gdn_gather_wait_counter")
+        return self.out[step % 2]
+
+    def close(self) -> None:
+        for p in self._opened:
+            self._lib.gdn_ipc_close(p)
+        self._opened = []
+
+
 def gdn_prefill_seqpar(q, k, v, g, beta, initial_state=None, *, group=None, scale: float = 1.0):
     """Sequence-parallel GDN prefill: rank j of the group holds the j-th
     contiguous T-segment of every sequence (q, k [B, T_j, Hqk, d], v [B, T_j,

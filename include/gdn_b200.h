@@ -84,6 +84,7 @@ enum {
   GDN_DEVERR_EMPTY_TIMEOUT = 1u << 1, /* producer waited too long for a free slot */
   GDN_DEVERR_MMA_TIMEOUT = 1u << 2,   /* tensor-core completion never signalled   */
   GDN_DEVERR_DRAIN_TIMEOUT = 1u << 3, /* copies in flight never landed on abort   */
+  GDN_DEVERR_PEER_TIMEOUT = 1u << 4,  /* a peer never released an output slot     */
 };
 
 /*
@@ -126,7 +127,41 @@ typedef struct {
   int64_t z_sb, z_sh;   /* element strides of z                              */
   const float* norm_weight; /* [d_v] fp32 RMSNorm weight                     */
   float norm_eps;       /* RMSNorm epsilon                                   */
+  const struct gdn_peer_out* peer_out; /* optional fused output all-gather   */
+                        /* over NVLink (value-head-sharded decode); NULL = none */
 } gdn_decode_args_t;
+
+/*
+ * Fused output all-gather of value-head-sharded decode (one process per GPU,
+ * rank r owning a contiguous range of value heads).  Every rank holds its own
+ * full output buffer [B, Hv_total, d_v] (two of them, used by alternate
+ * steps); `o` of the decode args points at this rank's head range inside the
+ * local buffer of the step's slot (o_sb = Hv_total * d_v, o_sh = d_v), and
+ * o_peer[i] at the same offset inside peer i's buffer of that slot, mapped
+ * into this process (CUDA IPC).  The decode kernel stores every output row to
+ * the local buffer and to each peer with plain stores over NVLink (no copy
+ * engine, no collective, no TMA multicast), then:
+ *   - arrival: the CTA that finishes last adds 1 to every rank's
+ *     arrive[] counter (system-scope atomics after a system fence), so rank j
+ *     has all outputs of step s once its counter reaches s * n_ranks;
+ *   - reuse of a slot: at the start of step s this rank writes s - 1 into
+ *     slot `rank` of every rank's free[] array ("I have consumed step s - 1");
+ *     before its first output store of step s a CTA waits, bounded, until
+ *     every entry of its own free[] is >= s - 2 (the slot's previous step was
+ *     consumed everywhere).  Reads of step s's gathered outputs must therefore
+ *     be ordered before this rank's next decode launch.
+ * A wait that runs out sets GDN_DEVERR_PEER_TIMEOUT in the status word.
+ */
+typedef struct gdn_peer_out {
+  void* o_peer[7];          /* peers' output bases (this rank's head offset)  */
+  uint32_t* arrive[8];      /* every rank's arrival counter (self included)   */
+  uint32_t* free_flags[8];  /* every rank's free[n_ranks] array               */
+  uint32_t* cta_done;       /* local counter of finished CTAs (monotonic)     */
+  int32_t n_ranks;          /* 2..8                                           */
+  int32_t rank;             /* this rank's index                              */
+  uint32_t step;            /* 1-based step number, +1 per decode launch      */
+  int32_t reserved;
+} gdn_peer_out_t;
 
 /*
  * Chunked prefill over T tokens.  Tensors are contiguous [B, T, H, d]
@@ -286,6 +321,12 @@ int gdn_gather_push(const void* src, size_t bytes, void* const* peer_dst,
 /* Makes `stream` wait (on the GPU front end) until flags[i] >= value for all
  * i < n. */
 int gdn_gather_wait(const uint32_t* flags, int32_t n, uint32_t value, gdn_stream_t stream);
+
+/* On `stream`: waits (a one-thread kernel, bounded; a timeout sets
+ * GDN_DEVERR_PEER_TIMEOUT in *status) until *counter >= target, for the
+ * arrival counter of the fused output all-gather (gdn_peer_out_t.arrive). */
+int gdn_gather_wait_counter(const uint32_t* counter, uint32_t target, uint32_t* status,
+                            gdn_stream_t stream);
 
 #ifdef __cplusplus
 }

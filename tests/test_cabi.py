@@ -40,20 +40,24 @@ def test_struct_layout_matches_header(pkg, tmp_path):
     src = tmp_path / "layout.c"
     fields_d = [f for f, _ in pkg._lib.DecodeArgs._fields_]
     fields_p = [f for f, _ in pkg._lib.PrefillArgs._fields_]
+    fields_o = [f for f, _ in pkg._lib.PeerOut._fields_]
     body = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
             'printf("%zu\\n", sizeof(gdn_decode_args_t));',
-            'printf("%zu\\n", sizeof(gdn_prefill_args_t));']
+            'printf("%zu\\n", sizeof(gdn_prefill_args_t));',
+            'printf("%zu\\n", sizeof(gdn_peer_out_t));']
     body += [f'printf("%zu\\n", offsetof(gdn_decode_args_t, {f}));' for f in fields_d]
     body += [f'printf("%zu\\n", offsetof(gdn_prefill_args_t, {f}));' for f in fields_p]
+    body += [f'printf("%zu\\n", offsetof(gdn_peer_out_t, {f}));' for f in fields_o]
     body += ["return 0;}"]
     src.write_text("\n".join(body))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", str(src), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
                                            check=True).stdout.split()]
-    D, P = pkg._lib.DecodeArgs, pkg._lib.PrefillArgs
-    expect = [ctypes.sizeof(D), ctypes.sizeof(P)]
+    D, P, O = pkg._lib.DecodeArgs, pkg._lib.PrefillArgs, pkg._lib.PeerOut
+    expect = [ctypes.sizeof(D), ctypes.sizeof(P), ctypes.sizeof(O)]
     expect += [getattr(D, f).offset for f in fields_d] + [getattr(P, f).offset for f in fields_p]
+    expect += [getattr(O, f).offset for f in fields_o]
     assert vals == expect
 
 

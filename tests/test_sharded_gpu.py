@@ -172,3 +172,58 @@ def test_sequence_parallel_prefill_two_gpus():
     o = np.concatenate([res[0][0], res[1][0]], axis=1)
     np.testing.assert_allclose(o, o_ref, rtol=2e-2, atol=1e-2)
     assert np.abs(res[1][1] - s_ref).max() < 1e-3
+
+
+def _fused_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        pkg = graft.package()
+        inputs = graft.submodule("inputs")
+        sh = graft.submodule("sharded")
+        dev = torch.device("cuda", rank)
+        x = inputs.make_decode_inputs(STEPS, B, HQK, HV, D, seed=23)
+        s = sh.shard_heads(HV, HQK, world, rank)
+        hv = s.h1 - s.h0
+        state = x.state[:, s.h0:s.h1].contiguous().to(dev)
+        fg = sh.FusedGather(B, HV, D, s.h0, hv, torch.bfloat16, dev)
+        outs = []
+        for t in range(STEPS):
+            ins = [x.q[t, :, s.hq0:s.hq1], x.k[t, :, s.hq0:s.hq1], x.v[t, :, s.h0:s.h1],
+                   x.g[t, :, s.h0:s.h1], x.beta[t, :, s.h0:s.h1]]
+            ins = [u.contiguous().to(dev) for u in ins]
+            pair = [fg.decode_step(slot, *ins, state) for slot in range(2)]
+            step = fg.launch(pair)
+            full = fg.wait(step)
+            outs.append(full.float().cpu())  # read before the next launch
+        pkg.check_device_status(dev)
+        states = [torch.empty_like(state) for _ in range(world)]
+        dist.all_gather(states, state)
+        dist.barrier()
+        fg.close()
+        if rank == 0:
+            q.put((torch.stack(outs).numpy(), torch.cat([t.cpu() for t in states], 1).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_fused_gather_decode_two_gpus_matches_oracle(orc, inputs):
+    """Decode with the output all-gather fused into the kernel: every step's
+    gathered [B, Hv, d] on rank 0 and the state shards against the oracle."""
+    x = inputs.make_decode_inputs(STEPS, B, HQK, HV, D, seed=23)
+    ref_o, ref_s = orc.gdn_decode_steps(x.q, x.k, x.v, x.g, x.beta, x.state)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    o, s = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    np.testing.assert_allclose(o, ref_o, rtol=O_RTOL, atol=O_ATOL)
+    assert np.abs(s - ref_s).max() < S_ATOL
