@@ -138,6 +138,11 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
     fence_mbar_init();
   }
   __syncthreads();
+  // The prologue above may overlap the previous kernel in the stream; every
+  // global access below comes after it has completed (inputs and the state
+  // may be its outputs).
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == Tr::kConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -499,8 +504,23 @@ static int launch_decode_impl(const gdn_decode_args_t& a, cudaStream_t stream) {
   int ctas = (di.sm_count - (a.sm_reserve > 0 ? a.sm_reserve : 0)) * Tr::kCtasPerSm;
   if (ctas < 1) ctas = 1;
   const int64_t grid64 = p.total_slabs < ctas ? p.total_slabs : ctas;
-  kern<<<static_cast<unsigned>(grid64), Tr::kThreads, smem, stream>>>(p, map);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  // programmatic dependent launch: this kernel's prologue (barrier set-up)
+  // overlaps the tail of the previous kernel in the stream
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid64));
+  cfg.blockDim = dim3(Tr::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, p, map) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_LAUNCH;
+  }
+  return GDN_OK;
 }
 
 static int validate_decode(const gdn_decode_args_t* a, bool kda) {

@@ -316,6 +316,11 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
       bv = load_any(a.beta, gi, a.beta_dtype);
     }
   };
+  // With programmatic dependent launch this kernel may start while the
+  // previous kernel in the stream drains: wait for it before the first
+  // global read, then let the state-pass kernel start its own prologue.
+  pdl_wait();
+  pdl_launch_dependents();
   float gv0, bv0;
   load_gate(0, gv0, bv0);
   if (warp == 0) tc::tmem_alloc(tmem_holder, 64);
@@ -684,7 +689,11 @@ __global__ void __launch_bounds__(state::kThreads, 1)
       tc::tma_load_4d(smem + kV + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
     bulk_g2s(smem + kTw, recs + static_cast<size_t>(n) * kWsUnit + kWsTw, 16384, bar);
   };
+  // Launched as a programmatic dependent of the intra kernel: everything up
+  // to here (and the state warps' initial-state load) overlaps its tail; the
+  // workspace and the inputs are read only after pdl_wait().
   if (tid == 2 * kGroupThreads) {
+    pdl_wait();
     for (int n = 0; n < 3 && n < nchunks; ++n) issue_kqp(n);
     issue_twu(0);
   }
@@ -692,6 +701,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   if (warp < 4) {
     // ================================================================ W group
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    pdl_wait();
     const int k = warp * 32 + lane;  // W^T row (d_k) this thread converts
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
@@ -736,6 +746,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   } else if (warp < 8) {
     // ================================================================ O group
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    pdl_wait();
     const int ot = tid - kGroupThreads;  // 0..127
     const int dv = (warp & 3) * 32 + lane;
     IO* o = static_cast<IO*>(a.o);
@@ -843,6 +854,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
 #pragma unroll
     for (int j = 0; j < 64; ++j)
       S[j] = a.initial_state ? a.initial_state[state_off + static_cast<size_t>(k0 + j) * kD + dv] : 0.f;
+    // the initial state is not an output of the intra kernel (whose own
+    // predecessor completed before it let this kernel start)
+    pdl_wait();
     auto write_st = [&]() {  // bf16 S^T into TMEM: lane dv, packed d_k pairs
 #pragma unroll
       for (int cb = 0; cb < 2; ++cb) {
@@ -1022,8 +1036,21 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   const unsigned n1 = static_cast<unsigned>(a.B * a.Hqk * p.nchunks);
   k1<<<n1, intra::kThreads, intra::kSmemAlloc, stream>>>(p, mq, mk);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
-  k2<<<static_cast<unsigned>(a.B * a.Hv), state::kThreads, state::kSmemAlloc, stream>>>(p, mq, mk, mv);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
+  cfg.blockDim = dim3(state::kThreads);
+  cfg.dynamicSmemBytes = state::kSmemAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k2, p, mq, mk, mv) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_LAUNCH;
+  }
+  return GDN_OK;
 }
 
 int validate(const gdn_prefill_args_t* a) {

@@ -25,6 +25,16 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// ------------------------------------------------------- programmatic launch
+// With programmatic dependent launch the next kernel in the stream may start
+// its prologue while this one drains.  launch_dependents allows that early
+// start; wait blocks until the preceding kernel has completed and its memory
+// is visible (a no-op when the kernel was launched without the attribute).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
