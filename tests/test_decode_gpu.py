@@ -260,12 +260,15 @@ def test_fused_layer_preprocessing(pkg, inputs, orc):
 
 
 @pytest.mark.parametrize("B,steps", [(8, 64), (64, 8), (10, 4)])
-def test_fp16_state_within_tolerance(pkg, inputs, orc, B, steps):
-    """Optional fp16 state (half the streamed bytes, fp32 arithmetic) against
-    the fp32 recurrence.  Outputs meet the BASELINE bf16 tolerance; the state
-    does NOT meet the BASELINE 1e-3 gate after 64 steps (1.25e-3 measured), so
-    this option is off by default and checked here against its own bound
-    (2e-3 max-abs).  Covers 32-, 64- and 128-column slabs."""
+def test_fp16_state_characterisation(pkg, inputs, orc, B, steps):
+    """Characterisation (not a parity test) of the optional fp16 state (half
+    the streamed bytes, fp32 arithmetic) against the fp32 recurrence.  Outputs
+    meet the BASELINE bf16 tolerance.  The state cannot meet the BASELINE 1e-3
+    max-abs gate: at |S| near 1.1 (reached after 64 steps) one fp16 rounding
+    alone is up to 4.9e-4, and after 64 steps the error is 1.25e-3 with
+    round-to-nearest (stochastic rounding, emulated, is worse: 1.6e-3).  The
+    option is therefore off by default; this test pins its measured error
+    below 2e-3.  Covers 32-, 64- and 128-column slabs."""
     x = inputs.make_decode_inputs(steps, B, 16, 32, 128, seed=40 + B)
     o_ref, s_ref = orc.gdn_decode_steps(x.q, x.k, x.v, x.g, x.beta, x.state)
     st = x.state.to(DEV, torch.float16)
