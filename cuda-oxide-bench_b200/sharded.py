@@ -330,14 +330,16 @@ def gdn_prefill_seqpar(q, k, v, g, beta, initial_state=None, *, group=None, scal
 
     The delta-rule recurrence is affine in the state over a segment,
     S_end = M S_start + L, with M = prod_t a_t (I - beta_t k_t k_t^T) (d_k x d_k)
-    and L the segment's state from zero.  Each rank obtains M by running the
-    chunked prefill from the identity state with v = 0, and L by running it
-    from zero; one all-gather exchanges (M_j, L_j); each rank scans the
-    segment start states in fp32 and re-runs its segment from its start state
-    for exact outputs.  Three prefills of length T/N per rank plus an
-    all-gather of 2 x [B, Hv, d, d] fp32.
-    ``initial_state`` (the state before segment 0) must be given on every rank
-    or on none.
+    and L the segment's state from zero.  A middle rank obtains M by running
+    the chunked prefill from the identity state with v = 0, and L by running
+    it from zero.  Rank 0 without an initial state starts from zero, so its
+    segment run already yields L_0 (and M_0 is never needed); the last rank's
+    (M, L) are needed by nobody.  One all-gather exchanges the (M_j, L_j);
+    each rank scans the segment start states in fp32 and runs its segment from
+    its start state for exact outputs.  The critical path is three prefills
+    of length T/N (two for N = 2) plus an all-gather of 2 x [B, Hv, d, d]
+    fp32.  ``initial_state`` (the state before segment 0) must be given on
+    every rank or on none.
     """
     from .api import gdn_prefill
     world = dist.get_world_size(group)
@@ -345,17 +347,27 @@ def gdn_prefill_seqpar(q, k, v, g, beta, initial_state=None, *, group=None, scal
     B, T, _, dk = q.shape
     Hv, dv = v.shape[2], v.shape[3]
     if dk != dv:
-        raise ValueError("sequence-parallel prefill needs d_k == d_v (M is d_k x d_k)")
+        raise ValueError("sequence-parallel prefill needs d_k == d_v (M is d_k x d_v)")
     dev = q.device
-    eye = torch.eye(dk, dtype=torch.float32, device=dev).expand(B, Hv, dk, dk).contiguous()
-    _, M = gdn_prefill(q, k, torch.zeros_like(v), g, beta, eye, scale=scale)
-    _, L = gdn_prefill(q, k, v, g, beta, None, scale=scale)
-    ML = torch.stack([M, L])                                        # [2, B, Hv, d, d]
+    zero_start = initial_state is None
+    ML = torch.zeros((2, B, Hv, dk, dv), dtype=torch.float32, device=dev)
+    first = None
+    if rank == 0 and zero_start:
+        first = gdn_prefill(q, k, v, g, beta, None, scale=scale)  # its end state is L_0
+        ML[1].copy_(first[1])
+    elif rank < world - 1:
+        eye = torch.eye(dk, dtype=torch.float32, device=dev).expand(B, Hv, dk, dk).contiguous()
+        gdn_prefill(q, k, torch.zeros_like(v), g, beta, eye, scale=scale, final_state=ML[0])
+        gdn_prefill(q, k, v, g, beta, None, scale=scale, final_state=ML[1])
     allml = torch.empty((world,) + tuple(ML.shape), dtype=ML.dtype, device=dev)
     dist.all_gather_into_tensor(allml.view(-1), ML.reshape(-1), group=group)
-    S = (initial_state.float() if initial_state is not None
+    if first is not None:
+        return first
+    S = (initial_state.float() if not zero_start
          else torch.zeros((B, Hv, dk, dv), dtype=torch.float32, device=dev))
     for j in range(rank):  # start state of this rank's segment (fp32 matmuls)
-        S = torch.matmul(allml[j, 0], S) + allml[j, 1]
-    o, S_end = gdn_prefill(q, k, v, g, beta, S.contiguous(), scale=scale)
-    return o, S_end
+        if j == 0 and zero_start:
+            S = allml[0, 1].clone()
+        else:
+            S = torch.matmul(allml[j, 0], S) + allml[j, 1]
+    return gdn_prefill(q, k, v, g, beta, S.contiguous(), scale=scale)

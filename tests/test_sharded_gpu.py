@@ -131,7 +131,7 @@ def test_copy_engine_gather_two_gpus():
     assert res == {0: True, 1: True}
 
 
-def _seqpar_worker(rank, world, port, q):
+def _seqpar_worker(rank, world, port, q, with_init=True):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
@@ -143,7 +143,7 @@ def _seqpar_worker(rank, world, port, q):
         S0 = torch.randn((1, 4, 128, 128), generator=torch.Generator().manual_seed(3)) * 0.02
         cut = [0, 128, 300]  # uneven segments, the second one ragged
         seg = [t[:, cut[rank]:cut[rank + 1]].contiguous().cuda() for t in (p.q, p.k, p.v, p.g, p.beta)]
-        o, S = sh.gdn_prefill_seqpar(*seg, S0.cuda())
+        o, S = sh.gdn_prefill_seqpar(*seg, S0.cuda() if with_init else None)
         q.put((rank, o.float().cpu().numpy(), S.cpu().numpy()))
         dist.barrier()
     finally:
@@ -152,13 +152,15 @@ def _seqpar_worker(rank, world, port, q):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
-def test_sequence_parallel_prefill_two_gpus():
+@pytest.mark.parametrize("with_init", [True, False])
+def test_sequence_parallel_prefill_two_gpus(with_init):
     """T split over two GPUs: outputs of both segments and the final state
-    match the sequential recurrence over the whole sequence."""
+    match the sequential recurrence over the whole sequence (with an initial
+    state, and from zero, where rank 0's own run supplies its segment map)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_seqpar_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_seqpar_worker, args=(r, 2, port, q, with_init)) for r in range(2)]
     for p in procs:
         p.start()
     res = {r: (o, S) for r, o, S in (q.get(timeout=300) for _ in range(2))}
@@ -168,7 +170,7 @@ def test_sequence_parallel_prefill_two_gpus():
     inputs = graft.submodule("inputs")
     p = inputs.make_prefill_inputs(1, 300, 2, 4, 128, seed=9)
     S0 = torch.randn((1, 4, 128, 128), generator=torch.Generator().manual_seed(3)) * 0.02
-    o_ref, s_ref = graft.oracle().gdn_prefill(p.q, p.k, p.v, p.g, p.beta, S0)
+    o_ref, s_ref = graft.oracle().gdn_prefill(p.q, p.k, p.v, p.g, p.beta, S0 if with_init else None)
     o = np.concatenate([res[0][0], res[1][0]], axis=1)
     np.testing.assert_allclose(o, o_ref, rtol=2e-2, atol=1e-2)
     assert np.abs(res[1][1] - s_ref).max() < 1e-3
