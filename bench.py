@@ -262,8 +262,8 @@ def run_gpu(args, world, rank, local):
         gstep = [0]
 
     def gather(i):
-        if fused:
-            return  # done inside the decode kernel
+        if fused or gmode == "none":
+            return  # done inside the decode kernel (or not at all)
         if world > 1 and ce:
             gstep[0] += 1
             ms_ = torch.cuda.current_stream(dev)
@@ -283,6 +283,8 @@ def run_gpu(args, world, rank, local):
                                                        async_op=True)
 
     def settle(i):
+        if gmode == "none":
+            return
         if ce:
             ev = ev_out_free[i % 2]
             if ev is not None:
@@ -382,6 +384,8 @@ def run_gpu(args, world, rank, local):
 
     # ---- parity of one more step (and of its gather) against the C oracle
     def gathered(i):  # [N, B, hv, d] rank-major slot holding step i's gathered outputs
+        if gmode == "none":
+            return None
         if fused:
             return fg.wait(fg.step).view(B, world, hv, D).permute(1, 0, 2, 3)
         if ce:
@@ -422,7 +426,8 @@ def run_gpu(args, world, rank, local):
                    "io_dtype": "bf16", "state": "fp32 in place",
                    "parallelism": f"value-head shard x{world}" + (
                        {"ce": " + copy-engine all-gather of o", "nccl": " + NCCL all-gather of o",
-                        "fused": " + all-gather of o fused into the decode kernel (NVLink stores)"}[gmode]
+                        "fused": " + all-gather of o fused into the decode kernel (NVLink stores)",
+                        "none": " (diagnostic: no all-gather)"}[gmode]
                        if world > 1 else ""),
                    "l2": "inputs larger than L2 (4.3 GB state), no flush"},
         "tokens_per_s": round(B / (ms * 1e-3), 1),
@@ -442,7 +447,8 @@ def run_gpu(args, world, rank, local):
         "cuda_graph": graph is not None,
         "allgather_overlapped": world > 1 and not args.no_overlap,
         "allgather": {"ce": "copy-engine push over NVLink (IPC)", "nccl": "NCCL",
-                      "fused": "decode kernel stores into every rank's buffer over NVLink (IPC)"}[gmode]
+                      "fused": "decode kernel stores into every rank's buffer over NVLink (IPC)",
+                      "none": None}[gmode]
                      if world > 1 else None,
         "sm_reserve": res,
         "clocks": clk.summary(),
@@ -484,7 +490,7 @@ def decode_parity(orc, toks, state, last_out, launch, gather, settle, join, gath
     err_s = float(np.abs(S1 - s_ref).max())
     bad = max(excess(o_dev, o_ref), err_s - s_atol)
     err_g = None
-    if world > 1:
+    if world > 1 and gathered(0) is not None:
         mine = torch.from_numpy(o_ref).to(dev)                       # [n, hv, d]
         allref = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=dev)
         dist.all_gather_into_tensor(allref.view(-1), mine.reshape(-1))
@@ -914,9 +920,10 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the decode leaves to the overlapped all-gather (N>1); default "
                          "by N: 16 at 2, 32 at 4, 48 at 8 (measured best on B200 x8)")
-    ap.add_argument("--gather", default="auto", choices=("auto", "fused", "ce", "nccl"),
+    ap.add_argument("--gather", default="auto", choices=("auto", "fused", "ce", "nccl", "none"),
                     help="N>1 output all-gather: fused into the decode kernel (NVLink stores, the "
-                         "default), copy engines over NVLink (ce) or NCCL")
+                         "default), copy engines over NVLink (ce) or NCCL; none (diagnostic: "
+                         "outputs stay on their rank)")
     ap.add_argument("--no-graph", action="store_true",
                     help="N>1: launch every step from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",

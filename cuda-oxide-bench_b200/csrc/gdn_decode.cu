@@ -407,17 +407,27 @@ __global__ void __launch_bounds__(DecodeTraits<DK, BV, KDA, SB>::kThreads,
       IO* o = static_cast<IO*>(a.o) + off;
       *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(ov);
       if (peer_ok) {
+        // the output-writing lanes (0 .. kColGroups-1 of warp 0) agree on one
+        // bounded wait for the slot, done once per CTA by lane 0
+        constexpr unsigned kMask = Tr::kColGroups == 32 ? 0xffffffffu : ((1u << Tr::kColGroups) - 1u);
         if (!peer_checked) {
           peer_checked = true;
-          if (!peer_slots_free(p.po)) {
-            peer_ok = false;
-            report(a.status, GDN_DEVERR_PEER_TIMEOUT);
+          int okw = 1;
+          if (cg == 0) {
+            okw = peer_slots_free(p.po) ? 1 : 0;
+            if (!okw) report(a.status, GDN_DEVERR_PEER_TIMEOUT);
           }
+          peer_ok = __shfl_sync(kMask, okw, 0) != 0;
         }
-        if (peer_ok) {
-          for (int i = 0; i < p.po.n_ranks - 1; ++i)
-            *reinterpret_cast<uint2*>(static_cast<IO*>(p.po.o_peer[i]) + off) =
-                *reinterpret_cast<const uint2*>(ov);
+        if (peer_ok) {  // 16-byte stores: even lanes send their and their neighbour's 4 outputs
+          const uint2 mine = *reinterpret_cast<const uint2*>(ov);
+          const uint32_t nx = __shfl_xor_sync(kMask, mine.x, 1);
+          const uint32_t ny = __shfl_xor_sync(kMask, mine.y, 1);
+          if ((cg & 1) == 0) {
+            const uint4 w = make_uint4(mine.x, mine.y, nx, ny);
+            for (int i = 0; i < p.po.n_ranks - 1; ++i)
+              *reinterpret_cast<uint4*>(static_cast<IO*>(p.po.o_peer[i]) + off) = w;
+          }
         }
       }
     }
