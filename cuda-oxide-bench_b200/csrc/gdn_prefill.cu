@@ -64,11 +64,11 @@ __device__ unsigned long long g_trace[64 * 16];
     if (blockIdx.x == 0 && (c) < 64 && (threadIdx.x & 127) == 0 && threadIdx.x < 384)        \
       g_trace[(c) * 16 + (ph)] = clock64();                                                    \
   } while (0)
-__device__ unsigned long long g_trace1[16 * 8];
+__device__ unsigned long long g_trace1[4096 * 8];
 __device__ unsigned long long g_cta[8192 * 5];  // start, end (globaltimer), smid, setup done, compute done
 #define TRACE1(ph)                                                                       \
   do {                                                                                   \
-    if (blockIdx.x < 16 && threadIdx.x == 0) g_trace1[blockIdx.x * 8 + (ph)] = clock64(); \
+    if (blockIdx.x < 4096 && threadIdx.x == 0) g_trace1[blockIdx.x * 8 + (ph)] = global_timer_ns(); \
   } while (0)
 #else
 #define TRACE1(ph) \
@@ -306,14 +306,25 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
 
   // raw gate and beta of token ht of value head (pair slot) hh, pair p0;
   // issued before anything else so that their latency overlaps the set-up
-  auto load_gate = [&](int p0, float& gv, float& bv) {
-    gv = 0.f;  // padded tokens: no decay, no update
-    bv = 0.f;
+  // (as raw bits: the conversion, and with it the wait for the load, happens
+  // at first use)
+  auto load_raw = [](const void* base, int64_t i, int dt) -> uint32_t {
+    if (dt == GDN_DT_F32) return __ldg(reinterpret_cast<const uint32_t*>(base) + i);
+    return __ldg(reinterpret_cast<const unsigned short*>(base) + i);
+  };
+  auto from_raw = [](uint32_t raw, int dt) -> float {
+    if (dt == GDN_DT_F32) return __uint_as_float(raw);
+    if (dt == GDN_DT_BF16) return __uint_as_float(raw << 16);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(raw)));
+  };
+  auto load_gate = [&](int p0, uint32_t& gv, uint32_t& bv) {
+    gv = 0u;  // padded tokens: no decay, no update (0 in every dtype)
+    bv = 0u;
     const int t = t0 + ht;
     if (p0 + hh < p.group && ht < kC && t < T) {
       const int64_t gi = (static_cast<int64_t>(b) * T + t) * a.Hv + hq * p.group + p0 + hh;
-      gv = load_any(a.g, gi, a.g_dtype);
-      bv = load_any(a.beta, gi, a.beta_dtype);
+      gv = load_raw(a.g, gi, a.g_dtype);
+      bv = load_raw(a.beta, gi, a.beta_dtype);
     }
   };
   // With programmatic dependent launch this kernel may start while the
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
   // global read, then let the state-pass kernel start its own prologue.
   pdl_wait();
   pdl_launch_dependents();
-  float gv0, bv0;
+  uint32_t gv0, bv0;
   load_gate(0, gv0, bv0);
   if (warp == 0) tc::tmem_alloc(tmem_holder, 64);
   if (tid == 0) {
@@ -348,13 +359,13 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
   int* sFast = reinterpret_cast<int*>(smem + kFlags) + hh;
   // The in-chunk cumulative log gate of value head (pair slot) hh of pair p0
   // and the exponentials derived from it (independent of the K/Q tiles).
-  auto gates = [&](int p0, float gv, float bv) {
+  auto gates = [&](int p0, uint32_t graw, uint32_t braw) {
     const bool active = p0 + hh < p.group;
     const int h = hq * p.group + p0 + hh;
     unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
     if (active && ht < kC) {
-      sG[ht] = gv;
-      sBeta[ht] = bv;
+      sG[ht] = from_raw(graw, a.g_dtype);
+      sBeta[ht] = from_raw(braw, a.beta_dtype);
     }
     tc::group_sync(bar, 128);
     if (active && w4 == 0) {  // in-chunk cumulative log gate; lane l owns tokens 2l, 2l+1
@@ -436,7 +447,7 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
       unsigned char* rec = p.ws + (static_cast<size_t>(b * a.Hv + h) * p.nchunks + c) * kWsUnit;
       if (p0 > 0) {
         if (ht == 64) bulk_wait_read();  // the previous pair's P tile has left
-        float gv, bv;
+        uint32_t gv, bv;
         load_gate(p0, gv, bv);
         gates(p0, gv, bv);
       }
@@ -468,11 +479,40 @@ __global__ void __launch_bounds__(intra::kThreads, GDN_K1_MINB)
             const float row_s = w4 < 2 ? bi : 1.f;
             const int lim = w4 < 2 ? i : i + 1;  // A: j < i; P: j <= i
             if (fast) {
+              // per 16-column block J: the warp's rows lie in blocks Ia and
+              // Ia + 1, so blocks below Ia need no mask and one product per
+              // element, blocks above Ia + 1 are zero, and only the two
+              // blocks at Ia, Ia + 1 take the general form
+              const int Ia = 2 * (w4 & 1);
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) {
-                const int j = cb * 32 + jj, J = j >> 4;
-                const float e = (J < I) ? rf[J < 3 ? J : 2] * sEe[j] : rd * sEs[j];
-                r[jj] = (j < lim) ? row_s * e * r[jj] : 0.f;
+              for (int jb = 0; jb < 2; ++jb) {
+                const int J = 2 * cb + jb;
+                float* rb = r + 16 * jb;
+                if (J < Ia) {
+                  const float f = row_s * rf[J < 3 ? J : 2];
+#pragma unroll
+                  for (int e4 = 0; e4 < 16; e4 += 4) {
+                    const float4 ee = *reinterpret_cast<const float4*>(sEe + 16 * J + e4);
+                    rb[e4] *= f * ee.x; rb[e4 + 1] *= f * ee.y; rb[e4 + 2] *= f * ee.z; rb[e4 + 3] *= f * ee.w;
+                  }
+                } else if (J > Ia + 1) {
+#pragma unroll
+                  for (int jj = 0; jj < 16; ++jj) rb[jj] = 0.f;
+                } else {
+                  const float fo = row_s * rf[J < 3 ? J : 2], fd = row_s * rd;
+#pragma unroll
+                  for (int e4 = 0; e4 < 16; e4 += 4) {
+                    const float4 ee = *reinterpret_cast<const float4*>(sEe + 16 * J + e4);
+                    const float4 es = *reinterpret_cast<const float4*>(sEs + 16 * J + e4);
+                    const float eo[4] = {ee.x, ee.y, ee.z, ee.w}, ed[4] = {es.x, es.y, es.z, es.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      const int j = 16 * J + e4 + q;
+                      const float e = (J < I) ? fo * eo[q] : fd * ed[q];
+                      rb[e4 + q] = (j < lim) ? e * rb[e4 + q] : 0.f;
+                    }
+                  }
+                }
               }
             } else {
 #pragma unroll
