@@ -194,16 +194,17 @@ __device__ __forceinline__ void solve_unit_lower(float* AT, float* M, int w, int
 #pragma unroll
     for (int i = 1; i < 16; ++i) {
       const float* row = AT + (bb + i) * kLd + bb;
-      float acc = 0.f;
+      // four partial sums (j mod 4) shorten the dependent FMA chain
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j4 = 0; j4 < i; j4 += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(row + j4);
-        acc = fmaf(a4.x, t[j4], acc);
-        if (j4 + 1 < i) acc = fmaf(a4.y, t[j4 + 1], acc);
-        if (j4 + 2 < i) acc = fmaf(a4.z, t[j4 + 2], acc);
-        if (j4 + 3 < i) acc = fmaf(a4.w, t[j4 + 3], acc);
+        acc[0] = fmaf(a4.x, t[j4], acc[0]);
+        if (j4 + 1 < i) acc[1] = fmaf(a4.y, t[j4 + 1], acc[1]);
+        if (j4 + 2 < i) acc[2] = fmaf(a4.z, t[j4 + 2], acc[2]);
+        if (j4 + 3 < i) acc[3] = fmaf(a4.w, t[j4 + 3], acc[3]);
       }
-      t[i] -= acc;
+      t[i] -= (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
     __syncwarp();
     if (lane < 16) {
