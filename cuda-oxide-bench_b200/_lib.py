@@ -46,6 +46,7 @@ EXPORTED = (
     "gdn_gather_push",
     "gdn_gather_wait",
     "gdn_gather_wait_counter",
+    "gdn_state_affine",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -165,6 +166,8 @@ def load(path: str | Path | None = None):
         L.gdn_gather_wait.argtypes = [vp, i32, ctypes.c_uint32, vp]
         L.gdn_gather_wait_counter.argtypes = [vp, ctypes.c_uint32, vp, vp]
         L.gdn_gather_wait_counter.restype = ctypes.c_int
+        L.gdn_state_affine.argtypes = [vp, vp, vp, vp, i32, i32, vp]
+        L.gdn_state_affine.restype = ctypes.c_int
         for fn in (L.gdn_ipc_handle, L.gdn_ipc_open, L.gdn_ipc_close, L.gdn_gather_push,
                    L.gdn_gather_wait):
             fn.restype = ctypes.c_int

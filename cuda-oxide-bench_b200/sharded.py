@@ -365,9 +365,18 @@ def gdn_prefill_seqpar(q, k, v, g, beta, initial_state=None, *, group=None, scal
         return first
     S = (initial_state.float() if not zero_start
          else torch.zeros((B, Hv, dk, dv), dtype=torch.float32, device=dev))
-    for j in range(rank):  # start state of this rank's segment (fp32 matmuls)
+    from . import _lib
+    L_ = _lib.load()
+    nmat = B * Hv
+    for j in range(rank):  # start state of this rank's segment: S <- M_j S + L_j (fp32)
         if j == 0 and zero_start:
             S = allml[0, 1].clone()
         else:
-            S = torch.matmul(allml[j, 0], S) + allml[j, 1]
+            S = S.contiguous()
+            S_next = torch.empty_like(S)
+            _lib.check(L_.gdn_state_affine(allml[j, 0].data_ptr(), allml[j, 1].data_ptr(),
+                                           S.data_ptr(), S_next.data_ptr(), nmat, dk,
+                                           torch.cuda.current_stream(dev).cuda_stream),
+                       "gdn_state_affine")
+            S = S_next
     return gdn_prefill(q, k, v, g, beta, S.contiguous(), scale=scale)

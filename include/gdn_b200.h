@@ -322,6 +322,14 @@ int gdn_gather_push(const void* src, size_t bytes, void* const* peer_dst,
  * i < n. */
 int gdn_gather_wait(const uint32_t* flags, int32_t n, uint32_t value, gdn_stream_t stream);
 
+/* S_out[i] = M[i] S_in[i] + L[i] for `count` row-major fp32 d x d matrices
+ * (d a multiple of 64; S_out must not alias S_in), in fp32: the start-state
+ * scan of the sequence-parallel prefill, which composes the affine maps
+ * S_end = M S_start + L of consecutive time segments.  No reference
+ * counterpart (the reference is single-GPU). */
+int gdn_state_affine(const float* M, const float* L, const float* S_in, float* S_out,
+                     int32_t count, int32_t d, gdn_stream_t stream);
+
 /* On `stream`: waits (a one-thread kernel, bounded; a timeout sets
  * GDN_DEVERR_PEER_TIMEOUT in *status) until *counter >= target, for the
  * arrival counter of the fused output all-gather (gdn_peer_out_t.arrive). */

@@ -82,3 +82,19 @@ def test_prefill_rejects_bad_sizes(pkg, inputs):
     p = inputs.make_prefill_inputs(1, 64, 1, 1, 64, seed=0)
     with pytest.raises(pkg.GDNError):
         pkg.gdn_prefill(*_dev(p))  # d = 64 is not a prefill size
+
+
+@pytest.mark.parametrize("count,d", [(3, 128), (2, 64), (1, 256)])
+def test_state_affine_matches_fp64(pkg, count, d):
+    """gdn_state_affine (the sequence-parallel start-state step) against
+    M S + L in float64."""
+    gen = torch.Generator().manual_seed(count + d)
+    M, L, S = (torch.randn((count, d, d), generator=gen) * 0.1 for _ in range(3))
+    Md, Ld, Sd = (t.to("cuda:0") for t in (M, L, S))
+    out = torch.empty_like(Sd)
+    rc = pkg._lib.load().gdn_state_affine(Md.data_ptr(), Ld.data_ptr(), Sd.data_ptr(),
+                                         out.data_ptr(), count, d,
+                                         torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    ref = (M.double() @ S.double() + L.double()).numpy()
+    assert np.abs(out.cpu().double().numpy() - ref).max() < 1e-5
