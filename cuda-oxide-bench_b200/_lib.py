@@ -40,6 +40,7 @@ EXPORTED = (
     "gdn_prefill_launch",
     "gdn_prefill_launch_noalloc",
     "kda_prefill_launch",
+    "kda_prefill_workspace_size",
     "gdn_ipc_handle",
     "gdn_ipc_open",
     "gdn_ipc_close",
@@ -158,6 +159,8 @@ def load(path: str | Path | None = None):
         L.gdn_prefill_launch_noalloc.restype = ctypes.c_int
         L.kda_prefill_launch.argtypes = [ctypes.POINTER(PrefillArgs), vp]
         L.kda_prefill_launch.restype = ctypes.c_int
+        L.kda_prefill_workspace_size.argtypes = [ctypes.POINTER(PrefillArgs)]
+        L.kda_prefill_workspace_size.restype = ctypes.c_size_t
         L.gdn_ipc_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
         L.gdn_ipc_open.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
         L.gdn_ipc_close.argtypes = [vp]

@@ -303,6 +303,19 @@ def _prefill_args(q, k, v, g, beta, initial_state, final_state, o, chunk, scale,
 _workspaces: dict[int, torch.Tensor] = {}
 
 
+def _workspace(dev, need: int, given):
+    """The caller's workspace tensor, or a per-device cached one of at least
+    ``need`` bytes (grown when a larger problem comes)."""
+    if given is not None:
+        return given
+    ws = _workspaces.get(dev.index)
+    if ws is None or ws.numel() < need:
+        _workspaces.pop(dev.index, None)
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        _workspaces[dev.index] = ws
+    return ws
+
+
 def gdn_prefill(q, k, v, g, beta, initial_state=None, *, chunk_size: int = 64,
                 scale: float = 1.0, out=None, final_state=None, workspace=None,
                 check: bool = False):
@@ -319,12 +332,7 @@ def gdn_prefill(q, k, v, g, beta, initial_state=None, *, chunk_size: int = 64,
     L = _lib.load()
     need = L.gdn_prefill_workspace_size(ctypes.byref(a))
     if need:
-        if workspace is None:
-            ws = _workspaces.get(dev.index)
-            if ws is None or ws.numel() < need:
-                ws = torch.empty(need, dtype=torch.uint8, device=dev)
-                _workspaces[dev.index] = ws
-            workspace = ws
+        workspace = _workspace(dev, need, workspace)
         a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     _lib.check(L.gdn_prefill_launch(ctypes.byref(a), _stream_ptr(dev)), "gdn_prefill")
     if check:
@@ -333,13 +341,20 @@ def gdn_prefill(q, k, v, g, beta, initial_state=None, *, chunk_size: int = 64,
 
 
 def kda_prefill(q, k, v, g, beta, initial_state=None, *, scale: float = 1.0, out=None,
-                final_state=None, check: bool = False):
+                final_state=None, form: str = "auto", workspace=None, check: bool = False):
     """KDA prefill over T tokens: T applications of the reference's
     naive_recurrent_kda_step (pytorch_reference_kda.py:42-71) with the state
     threaded through.  q, k [B,T,Hqk,d_k]; v [B,T,Hv,d_v]; g [B,T,Hv,d_k]
     per-channel log gate; beta [B,T,Hv].  Returns (o [B,T,Hv,d_v],
     final_state fp32 [B,Hv,d_k,d_v]).  ``final_state`` may be the
-    ``initial_state`` tensor (updated in place)."""
+    ``initial_state`` tensor (updated in place).
+
+    ``form``: "chunked" (tensor cores, 64-token chunks; d_k = d_v = 128 only),
+    "recurrent" (state on chip, CUDA cores; d in {64, 128, 256}) or "auto"
+    (chunked where it exists).  The chunked form uses a device workspace
+    (cached per device unless ``workspace`` is given)."""
+    if form not in ("auto", "chunked", "recurrent"):
+        raise GDNError(f"form must be 'auto', 'chunked' or 'recurrent', not {form!r}", 2)
     dev = _require_cuda(q, k, v, g, beta)
     B, T, _, dk = q.shape
     Hv, dv = v.shape[2], v.shape[3]
@@ -348,7 +363,15 @@ def kda_prefill(q, k, v, g, beta, initial_state=None, *, scale: float = 1.0, out
     if final_state is None:
         final_state = torch.empty((B, Hv, dk, dv), dtype=torch.float32, device=dev)
     a = _prefill_args(q, k, v, g, beta, initial_state, final_state, out, 0, scale, kda=True)
-    _lib.check(_lib.load().kda_prefill_launch(ctypes.byref(a), _stream_ptr(dev)), "kda_prefill")
+    L = _lib.load()
+    if form != "recurrent":
+        need = L.kda_prefill_workspace_size(ctypes.byref(a))
+        if not need and form == "chunked":
+            raise GDNError("the chunked KDA prefill needs d_k = d_v = 128", 2)
+        if need:
+            workspace = _workspace(dev, need, workspace)
+            a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    _lib.check(L.kda_prefill_launch(ctypes.byref(a), _stream_ptr(dev)), "kda_prefill")
     if check:
         check_device_status(dev)
     return out, final_state

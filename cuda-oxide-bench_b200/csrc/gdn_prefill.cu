@@ -89,6 +89,19 @@ constexpr uint32_t kWsVec = 24576;   // gamma[64], exp(G_C - G_j)[64] fp32
 constexpr uint32_t kWsUnit = 25088;
 static_assert(kWsUnit % 16 == 0 && kWsP % 16 == 0 && kWsVec % 16 == 0, "bulk-copy alignment");
 
+// Workspace record of the KDA (per-channel gate) prefill, one per (batch,
+// value head, chunk).  The per-channel decays cannot be applied as row
+// scales inside the state pass, so the intra kernel hands over operands that
+// already carry them (G: in-chunk cumulative log gate, per token and channel):
+constexpr uint32_t kKWsTu = 0;       // T diag(beta), K-major rows i             (8 KB)
+constexpr uint32_t kKWsP = 8192;     // (Q K^T)_ij over channels with exp(G_i - G_j), causal (8 KB)
+constexpr uint32_t kKWsWT = 16384;   // W^T = (T diag(beta) (K . exp(G)))^T, MN-major rows d_k (16 KB)
+constexpr uint32_t kKWsQT = 32768;   // (Q . exp(G))^T, MN-major rows d_k          (16 KB)
+constexpr uint32_t kKWsKd = 49152;   // K . exp(G_C - G) as f16, the K tile layout (16 KB)
+constexpr uint32_t kKWsVec = 65536;  // exp(G_C)[d_k] fp32                         (512 B)
+constexpr uint32_t kKWsUnit = 66048;
+static_assert(kKWsUnit % 16 == 0, "bulk-copy alignment");
+
 struct Params {
   gdn_prefill_args_t a;
   int32_t nchunks;
@@ -648,7 +661,9 @@ enum {
   kBarX = 9,       // V' = U - W S (and the first O term) done
   kBarS2 = 10,     // dS done
   kBarZO = 11,     // [2] O of a chunk complete (its K/Q/P slot is free)
-  kNumBars = 13,
+  kBarWT = 13,     // KDA: the W^T tile of a chunk landed (bulk)
+  kBarQT = 14,     // KDA: [2] the (Q . exp(G))^T tile of a chunk landed (bulk)
+  kNumBars = 16,
 };
 }  // namespace state
 
@@ -657,7 +672,7 @@ __device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
   return tc::pack2<BF16>(lo, hi);
 }
 
-template <bool BF16>
+template <bool BF16, bool KDA>
 __global__ void __launch_bounds__(state::kThreads, 1)
     state_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
                  const __grid_constant__ CUtensorMap map_k,
@@ -677,8 +692,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   const int b = bh / a.Hv, h = bh % a.Hv, hq = h / p.group;
   const int T = a.T;
   const int nchunks = p.nchunks;
-  const unsigned char* recs = p.ws + static_cast<size_t>(bh) * nchunks * kWsUnit;
-  auto pvec = [&](int c) {  // {gamma[64], decay[64]} of chunk c (in its K/Q/P slot)
+  constexpr uint32_t kUnit = KDA ? kKWsUnit : kWsUnit;
+  const unsigned char* recs = p.ws + static_cast<size_t>(bh) * nchunks * kUnit;
+  auto pvec = [&](int c) {  // GDN {gamma[64], decay[64]}, KDA exp(G_C)[128] of chunk c (in its K/Q/P slot)
     return reinterpret_cast<const float*>(smem + kP + (c % 3) * kPSlot + 8192);
   };
 
@@ -694,6 +710,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     mbar_init(&bars[kBarS2], 1);
     mbar_init(&bars[kBarZO], 1);
     mbar_init(&bars[kBarZO + 1], 1);
+    mbar_init(&bars[kBarWT], 1);
+    mbar_init(&bars[kBarQT], 1);
+    mbar_init(&bars[kBarQT + 1], 1);
     fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -704,31 +723,58 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, BF16);
   constexpr uint32_t kIdXZ = tc::idesc_f16(128, 128, false, true, BF16, true);
   constexpr uint32_t kIdOIneg = tc::idesc_f16(128, 64, false, false, BF16, true);
-  constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, BF16);
+  // KDA: dS^T = V'^T (K . exp(G_C - G)) takes f16 operands (the decayed keys
+  // keep 11 mantissa bits; V' enters as f16 hi + lo)
+  constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, KDA ? false : BF16);
 
-  auto issue_kqp = [&](int n) {  // K, Q (TMA), P and vectors (bulk) of chunk n into slot n % 3
+  // GDN: K, Q (TMA), P and vectors (bulk) of chunk n into slot n % 3.
+  // KDA: the decayed keys (in the K tile places), P and exp(G_C), all bulk.
+  auto issue_kqp = [&](int n) {
     const int slot = n % 3;
     uint64_t* bar = &bars[kBarKQP + slot];
-    mbar_arrive_expect_tx(bar, 4 * 8192 + 8192 + 512);
-    const int t0 = n * kC;
+    const unsigned char* rec = recs + static_cast<size_t>(n) * kUnit;
+    if constexpr (KDA) {
+      mbar_arrive_expect_tx(bar, 2 * 8192 + 8192 + 512);
 #pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {
-      unsigned char* kq = smem + kKQ + slot * kKQSlot + blk * kKQBlock;
-      tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, bar);
-      tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, bar);
+      for (int blk = 0; blk < 2; ++blk)
+        bulk_g2s(smem + kKQ + slot * kKQSlot + blk * kKQBlock, rec + kKWsKd + blk * 8192, 8192, bar);
+      bulk_g2s(smem + kP + slot * kPSlot, rec + kKWsP, 8192, bar);
+      bulk_g2s(smem + kP + slot * kPSlot + 8192, rec + kKWsVec, 512, bar);
+    } else {
+      mbar_arrive_expect_tx(bar, 4 * 8192 + 8192 + 512);
+      const int t0 = n * kC;
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        unsigned char* kq = smem + kKQ + slot * kKQSlot + blk * kKQBlock;
+        tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, bar);
+        tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, bar);
+      }
+      bulk_g2s(smem + kP + slot * kPSlot, rec + kWsP, 8192, bar);
+      bulk_g2s(smem + kP + slot * kPSlot + 8192, rec + kWsVec, 512, bar);
     }
-    const unsigned char* rec = recs + static_cast<size_t>(n) * kWsUnit;
-    bulk_g2s(smem + kP + slot * kPSlot, rec + kWsP, 8192, bar);
-    bulk_g2s(smem + kP + slot * kPSlot + 8192, rec + kWsVec, 512, bar);
   };
-  auto issue_twu = [&](int n) {  // V (TMA), T_w | T_u (bulk) of chunk n
+  auto issue_twu = [&](int n) {  // V (TMA), T_w | T_u (GDN) or T_u (KDA) (bulk) of chunk n
     uint64_t* bar = &bars[kBarTWU];
-    mbar_arrive_expect_tx(bar, 2 * 8192 + 16384);
+    mbar_arrive_expect_tx(bar, 2 * 8192 + (KDA ? 8192 : 16384));
     const int t0 = n * kC;
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk)
       tc::tma_load_4d(smem + kV + blk * kVBlock, &map_v, blk * 64, h, t0, b, bar);
-    bulk_g2s(smem + kTw, recs + static_cast<size_t>(n) * kWsUnit + kWsTw, 16384, bar);
+    if constexpr (KDA)
+      bulk_g2s(smem + kTu, recs + static_cast<size_t>(n) * kUnit + kKWsTu, 8192, bar);
+    else
+      bulk_g2s(smem + kTw, recs + static_cast<size_t>(n) * kUnit + kWsTw, 16384, bar);
+  };
+  // KDA: the W^T tile of chunk n (into kWQ, after X of chunk n - 1 read it)
+  // and the (Q . exp(G))^T tile of chunk n (into Q^T slot n & 1)
+  auto issue_wt = [&](int n) {
+    mbar_arrive_expect_tx(&bars[kBarWT], 16384);
+    bulk_g2s(smem + kWQ, recs + static_cast<size_t>(n) * kUnit + kKWsWT, 16384, &bars[kBarWT]);
+  };
+  auto issue_qt = [&](int n) {
+    uint64_t* bar = &bars[kBarQT + (n & 1)];
+    mbar_arrive_expect_tx(bar, 16384);
+    bulk_g2s(smem + kWQ + 16384 * (1 + (n & 1)), recs + static_cast<size_t>(n) * kUnit + kKWsQT, 16384, bar);
   };
   // Launched as a programmatic dependent of the intra kernel: everything up
   // to here (and the state warps' initial-state load) overlaps its tail; the
@@ -737,6 +783,9 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     pdl_wait();
     for (int n = 0; n < 3 && n < nchunks; ++n) issue_kqp(n);
     issue_twu(0);
+    if constexpr (KDA) {
+      for (int n = 0; n < 2 && n < nchunks; ++n) issue_qt(n);
+    }
   }
 
   if (warp < 4) {
@@ -745,7 +794,32 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     pdl_wait();
     const int k = warp * 32 + lane;  // W^T row (d_k) this thread converts
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
+    if constexpr (KDA) {
+      // KDA: W^T arrives precomputed (bulk); only U^T = V^T T_u^T is formed here
+      for (int c = 0; c < nchunks; ++c) {
+        const int slot = c & 1;
+        const uint32_t tmu = tmem + kTmUO + slot * 128;
+        if (!group_wait(&bars[kBarTWU], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
+        // the U slot was last used by chunk c - 2 and the W^T tile by X of c - 1
+        if (c >= 1 && !group_wait(&bars[kBarX], (c - 1) & 1, kBarW, kGroupThreads)) { ok = false; break; }
+        TRACE(c, 0);
+        if (tid == 0) {
+          issue_wt(c);
+          tc::fence_after_sync();
+#pragma unroll
+          for (int s = 0; s < 4; ++s)
+            tc::mma(tmu, tc::mnmajor_desc(sb + kV, kVBlock, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+          tc::commit(&bars[kBarHMma]);
+        }
+        if (!group_wait(&bars[kBarHMma], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
+        if (tid == 0 && c + 1 < nchunks) issue_twu(c + 1);  // V / T_u slot is free again
+        if (!group_wait(&bars[kBarWT], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
+        TRACE(c, 1);
+        tc::fence_before_sync();
+        mbar_arrive(&bars[kBarGo + slot]);
+        TRACE(c, 2);
+      }
+    } else for (int c = 0; c < nchunks; ++c) {
       const int slot = c & 1;
       const uint32_t kq = sb + kKQ + (c % 3) * kKQSlot;
       const uint32_t tmu = tmem + kTmUO + slot * 128;
@@ -838,7 +912,11 @@ __global__ void __launch_bounds__(state::kThreads, 1)
       if (!group_wait(&bars[kBarZO + (c & 1)], (c >> 1) & 1, kBarO, kGroupThreads)) return false;
       tc::fence_after_sync();
       if (ot == 0 && c + 3 < nchunks) issue_kqp(c + 3);  // every MMA of chunk c is done
-      if (c + 2 < nchunks && !scale_q(c + 2)) return false;
+      if constexpr (KDA) {
+        if (ot == 0 && c + 2 < nchunks) issue_qt(c + 2);  // Q^T slot c & 1 was last read by X of c
+      } else {
+        if (c + 2 < nchunks && !scale_q(c + 2)) return false;
+      }
       tc::group_sync(kBarO, kGroupThreads);  // every warp has read the Q tile reused below
       const uint32_t tmo = tmem + kTmUO + (c & 1) * 128 + 64;
       unsigned char* stage = smem + kKQ + ((c + 2) % 3) * kKQSlot + 8192;  // + (dv / 64) * kKQBlock
@@ -875,8 +953,11 @@ __global__ void __launch_bounds__(state::kThreads, 1)
     zero_o(1);
     bool ok = true;
     for (int c = 0; c < 2 && c < nchunks && ok; ++c) {
-      ok = scale_q(c);
-      if (ok) mbar_arrive(&bars[kBarGo + c]);
+      if constexpr (!KDA) ok = scale_q(c);  // KDA: the scaled Q^T tiles arrive by bulk copy
+      if (ok) {
+        tc::fence_before_sync();
+        mbar_arrive(&bars[kBarGo + c]);
+      }
     }
     for (int c = 0; c < nchunks && ok; ++c) {
       if (!outputs(c)) { ok = false; break; }
@@ -925,7 +1006,8 @@ __global__ void __launch_bounds__(state::kThreads, 1)
       bool mine = true;
       if (st == 0) {  // [V'^T | O^T] = [U^T | 0] - S^T [W^T | (diag(gamma) Q)^T]  (A = S^T from TMEM)
         mine = (c == 0 || mbar_wait_bounded(&bars[kBarSt], (c - 1) & 1)) &&
-               mbar_wait_bounded(&bars[kBarGo + slot], (c >> 1) & 1);
+               mbar_wait_bounded(&bars[kBarGo + slot], (c >> 1) & 1) &&
+               (!KDA || mbar_wait_bounded(&bars[kBarQT + slot], (c >> 1) & 1));
         TRACE(c, 4);
         if (mine) {
           tc::fence_after_sync();
@@ -939,7 +1021,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
       const float* vc = pvec(c);
       if (!group_wait(&bars[kBarX], c & 1, kBarState, kStateThreads, !mine)) { ok = false; break; }
       tc::fence_after_sync();
-      const float gC = vc[kC - 1];
+      const float gC = KDA ? 0.f : vc[kC - 1];
       TRACE(c, 5);
       {  // V' (TMEM) -> bf16 V'^T tile; V'' = V' exp(G_C - G_j) -> bf16 hi / lo
          // written back over the thread's own V' columns: for its 32 tokens,
@@ -960,11 +1042,17 @@ __global__ void __launch_bounds__(state::kThreads, 1)
             for (int e2 = 0; e2 < 2; ++e2) {
               const int e = q4 * 2 + e2;
               const float u0 = u[cb * 16 + 2 * e], u1 = u[cb * 16 + 2 * e + 1];
-              const float v0 = u0 * dd[2 * e2], v1 = u1 * dd[2 * e2 + 1];
               wp[e] = tc::pack2<BF16>(u0, u1);
-              const uint32_t hw = tc::pack2<BF16>(v0, v1);
-              wh[e] = hw;
-              wl[e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(hw), v1 - tc::unpack_hi<BF16>(hw));
+              if constexpr (KDA) {  // the decay sits in the keys; V' as f16 hi + lo
+                const uint32_t hw = tc::pack2<false>(u0, u1);
+                wh[e] = hw;
+                wl[e] = tc::pack2<false>(u0 - tc::unpack_lo<false>(hw), u1 - tc::unpack_hi<false>(hw));
+              } else {
+                const float v0 = u0 * dd[2 * e2], v1 = u1 * dd[2 * e2 + 1];
+                const uint32_t hw = tc::pack2<BF16>(v0, v1);
+                wh[e] = hw;
+                wl[e] = tc::pack2<BF16>(v0 - tc::unpack_lo<BF16>(hw), v1 - tc::unpack_hi<BF16>(hw));
+              }
             }
           }
           const int ch = half * 4 + cb * 2;
@@ -1014,8 +1102,19 @@ __global__ void __launch_bounds__(state::kThreads, 1)
           tc::tmem_ld16(tmem + lane_base + kTmDS + half * 64 + hb * 32 + 16,
                         *reinterpret_cast<float(*)[16]>(r + 16));
           tc::tmem_wait_ld();
+          if constexpr (KDA) {  // per-row decay exp(G_C)[d_k]
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) S[hb * 32 + jj] = fmaf(gC, S[hb * 32 + jj], r[jj]);
+            for (int j4 = 0; j4 < 32; j4 += 4) {
+              const float4 g4 = *reinterpret_cast<const float4*>(vc + k0 + hb * 32 + j4);
+              S[hb * 32 + j4] = fmaf(g4.x, S[hb * 32 + j4], r[j4]);
+              S[hb * 32 + j4 + 1] = fmaf(g4.y, S[hb * 32 + j4 + 1], r[j4 + 1]);
+              S[hb * 32 + j4 + 2] = fmaf(g4.z, S[hb * 32 + j4 + 2], r[j4 + 2]);
+              S[hb * 32 + j4 + 3] = fmaf(g4.w, S[hb * 32 + j4 + 3], r[j4 + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) S[hb * 32 + jj] = fmaf(gC, S[hb * 32 + jj], r[jj]);
+          }
         }
         write_st();
       }
@@ -1035,6 +1134,411 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
 }
 
+// ============================================================ KDA intra kernel
+// KDA (per-channel log gate g[t][c]) version of the intra kernel.  With G the
+// in-chunk cumulative log gate per channel, every pairwise factor
+// exp(G_ic - G_jc) now depends on the channel, so the decays go into the MMA
+// operands instead of scaling the product.  For row block I (tokens 16 I ..
+// 16 I + 15) and the reference point r_I = G at token 16 I:
+//   A_ij / beta_i = sum_c [k_ic exp(G_ic - r_Ic)] [k_jc exp(r_Ic - G_jc)]
+// The left factor is <= 1 for every row of block I; the right one is <= 1 for
+// j < 16 I and at most exp(in-block decay) on the diagonal block.  One MMA per
+// row block I (N = 16 (I + 1) columns, M = 128 rows [K-rows; Q-rows]) gives
+// the A and P rows of that block.  The remaining operands of the state pass
+// (W^T, (Q . exp(G))^T, the decayed keys K . exp(G_C - G) and exp(G_C)) are
+// formed here too, so the state kernel's per-chunk work is the GDN one.
+// Fast path (every |G| <= 80 in the chunk): two exponentials per element,
+// exp(G) and exp(-G), and products of per-channel block constants.  Otherwise
+// every factor is its own exponential of a non-positive argument, and the
+// diagonal blocks of A and P are summed directly from the gates (the
+// factored form could overflow there).
+namespace kintra {
+constexpr int kThreads = 256;
+constexpr uint32_t kKQ = 0;            // [K | Q] per d_k block (2 x 16 KB), scaled in place
+constexpr uint32_t kKQBlock = 16384;
+constexpr uint32_t kAT = 0;            // A -> T over the K/Q tiles once the products are done
+constexpr uint32_t kMs = 64 * kLd * 4; // 17408: solver scratch (4608 B), likewise
+constexpr uint32_t kKn = 32768;        // right factors of row block I: 16 (I + 1) rows each
+constexpr uint32_t kKnBytes = 40960;
+constexpr int kGLd = 130;              // slow path: G [64][kGLd] fp32 over the right factors
+constexpr uint32_t kGs = kKn;
+constexpr uint32_t kKg = kKn + kKnBytes;  // 73728: K . exp(G), 2 d_k blocks x 8 KB
+constexpr uint32_t kTu = kKg + 16384;     // 90112: P staging, then T_u
+constexpr uint32_t kBeta = kTu + 8192;    // 98304: beta[64]
+constexpr uint32_t kGb = kBeta + 256;     // G at tokens 0, 16, 32, 48 and 63, per channel [5][128]
+constexpr uint32_t kPart = kGb + 5 * 128 * 4;   // per-block gate sums [4][128]
+constexpr uint32_t kBars = kPart + 4 * 128 * 4;
+constexpr uint32_t kSmemBytes = kBars + 64;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
+constexpr uint32_t kTmCols = 256;      // A/P products at 8 I (I + 1) (160 columns), W^T at 192
+constexpr uint32_t kTmW = 192;
+__host__ __device__ constexpr uint32_t kn_off(int I) { return 2048u * I * (I + 1); }
+__host__ __device__ constexpr uint32_t kn_blk(int I) { return 2048u * (I + 1); }
+static_assert(kMs + 4608 <= kKn && 64 * kGLd * 4 <= kKnBytes && kn_off(4) == kKnBytes, "smem map");
+}  // namespace kintra
+
+template <bool BF16>
+__global__ void __launch_bounds__(kintra::kThreads, 2)
+    kda_intra_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
+                     const __grid_constant__ CUtensorMap map_k) {
+  using namespace kintra;
+  using IO = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);  // [0] TMA, [1] A/P MMA, [2] W MMA
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3);
+  const gdn_prefill_args_t& a = p.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per_c = a.B * a.Hv;
+  const int c = p.nchunks - 1 - static_cast<int>(blockIdx.x) / per_c;
+  const int bh = static_cast<int>(blockIdx.x) % per_c;
+  const int b = bh / a.Hv, h = bh % a.Hv, hq = h / p.group;
+  const int T = a.T, t0 = c * kC;
+  unsigned char* rec = p.ws + (static_cast<size_t>(bh) * p.nchunks + c) * kKWsUnit;
+  // build-phase role: token block J, d_k block kb, channels ch, ch + 1
+  const int J = warp >> 1, kb = warp & 1;
+  const int ch = kb * 64 + 2 * lane;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  // raw gates of this thread's 16 tokens and 2 channels (converted at first use)
+  uint32_t gr0[16], gr1[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    gr0[r] = 0u;  // padded tokens: no decay
+    gr1[r] = 0u;
+    const int t = t0 + 16 * J + r;
+    if (t < T) {
+      const int64_t gi = ((static_cast<int64_t>(b) * T + t) * a.Hv + h) * kD + ch;
+      if (a.g_dtype == GDN_DT_F32) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.g) + (gi >> 1));
+        gr0[r] = u.x;
+        gr1[r] = u.y;
+      } else {
+        gr0[r] = __ldg(reinterpret_cast<const uint32_t*>(a.g) + (gi >> 1));
+      }
+    }
+  }
+  uint32_t braw = 0u;
+  if (tid < kC && t0 + tid < T) {
+    const int64_t bi = (static_cast<int64_t>(b) * T + t0 + tid) * a.Hv + h;
+    braw = a.beta_dtype == GDN_DT_F32 ? __ldg(reinterpret_cast<const uint32_t*>(a.beta) + bi)
+                                      : __ldg(reinterpret_cast<const unsigned short*>(a.beta) + bi);
+  }
+  auto gate = [&](uint32_t raw, bool hi) -> float {
+    if (a.g_dtype == GDN_DT_F32) return __uint_as_float(raw);
+    const uint32_t bits = hi ? (raw >> 16) : (raw & 0xFFFFu);
+    if (a.g_dtype == GDN_DT_BF16) return __uint_as_float(bits << 16);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+  };
+
+  if (warp == 0) tc::tmem_alloc(tmem_holder, kTmCols);
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], 4 * 8192);
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      unsigned char* kq = smem + kKQ + blk * kKQBlock;
+      tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
+      tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
+    }
+  }
+
+  // ---- in-chunk cumulative log gate per channel (while K / Q are in flight)
+  float* sBeta = reinterpret_cast<float*>(smem + kBeta);
+  float* sGb = reinterpret_cast<float*>(smem + kGb);
+  float* sPart = reinterpret_cast<float*>(smem + kPart);
+  float G0[16], G1[16];
+  {
+    float run0 = 0.f, run1 = 0.f;
+    const bool f32 = a.g_dtype == GDN_DT_F32;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      run0 += gate(gr0[r], false);
+      run1 += f32 ? gate(gr1[r], false) : gate(gr0[r], true);
+      G0[r] = run0;
+      G1[r] = run1;
+    }
+    *reinterpret_cast<float2*>(sPart + J * 128 + ch) = make_float2(run0, run1);
+    if (tid < kC) {
+      sBeta[tid] = a.beta_dtype == GDN_DT_F32   ? __uint_as_float(braw)
+                   : a.beta_dtype == GDN_DT_BF16 ? __uint_as_float(braw << 16)
+                                                 : __half2float(__ushort_as_half(static_cast<unsigned short>(braw)));
+    }
+  }
+  __syncthreads();
+  bool in_range = true;
+  {
+    float o0 = 0.f, o1 = 0.f;
+    for (int jb = 0; jb < J; ++jb) {
+      const float2 pp = *reinterpret_cast<const float2*>(sPart + jb * 128 + ch);
+      o0 += pp.x;
+      o1 += pp.y;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      G0[r] += o0;
+      G1[r] += o1;
+      in_range = in_range && fabsf(G0[r]) <= 80.f && fabsf(G1[r]) <= 80.f;
+    }
+    *reinterpret_cast<float2*>(sGb + J * 128 + ch) = make_float2(G0[0], G1[0]);
+    if (J == 3) *reinterpret_cast<float2*>(sGb + 4 * 128 + ch) = make_float2(G0[15], G1[15]);
+  }
+  const bool fast = !__syncthreads_or(!in_range);  // also publishes sGb / sBeta
+
+  // ---- scaled operands
+  bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], 0));
+  if (ok) {
+    const float2 gc = *reinterpret_cast<const float2*>(sGb + 4 * 128 + ch);
+    float gbI0[4], gbI1[4];
+#pragma unroll
+    for (int I = 0; I < 4; ++I) {
+      const float2 v = *reinterpret_cast<const float2*>(sGb + I * 128 + ch);
+      gbI0[I] = v.x;
+      gbI1[I] = v.y;
+    }
+    // fast-path constants: exp(-r_J), exp(G_C), exp(r_I)
+    float yb0 = 0.f, yb1 = 0.f, xc0 = 0.f, xc1 = 0.f, xb0[4] = {}, xb1[4] = {};
+    if (fast) {
+      yb0 = __expf(-gbI0[J]);
+      yb1 = __expf(-gbI1[J]);
+#pragma unroll
+      for (int I = 0; I < 4; ++I) {
+        xb0[I] = __expf(gbI0[I]);
+        xb1[I] = __expf(gbI1[I]);
+      }
+    }
+    xc0 = expf(gc.x);  // the state's per-chunk decay: full-accuracy exponential
+    xc1 = expf(gc.y);
+    if (J == 3) *reinterpret_cast<float2*>(rec + kKWsVec + ch * 4) = make_float2(xc0, xc1);
+    float qg0[16], qg1[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int i = 16 * J + r;
+      const uint32_t off = tc::sw128_offset(i, lane >> 2) + (lane & 3) * 4;
+      uint32_t* kp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + off);
+      uint32_t* qp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + 8192 + off);
+      const uint32_t kw = *kp, qw = *qp;
+      const float k0 = tc::unpack_lo<BF16>(kw), k1 = tc::unpack_hi<BF16>(kw);
+      const float q0 = tc::unpack_lo<BF16>(qw), q1 = tc::unpack_hi<BF16>(qw);
+      float x0, x1, ea0, ea1, kd0, kd1, kn0[4], kn1[4];
+      if (fast) {
+        x0 = __expf(G0[r]);
+        x1 = __expf(G1[r]);
+        const float y0 = __expf(-G0[r]), y1 = __expf(-G1[r]);
+        ea0 = x0 * yb0;
+        ea1 = x1 * yb1;
+        kd0 = y0 * xc0;
+        kd1 = y1 * xc1;
+#pragma unroll
+        for (int I = 0; I < 4; ++I) {
+          kn0[I] = y0 * xb0[I];
+          kn1[I] = y1 * xb1[I];
+        }
+      } else {
+        x0 = __expf(G0[r]);
+        x1 = __expf(G1[r]);
+        ea0 = __expf(G0[r] - gbI0[J]);
+        ea1 = __expf(G1[r] - gbI1[J]);
+        kd0 = __expf(gc.x - G0[r]);
+        kd1 = __expf(gc.y - G1[r]);
+#pragma unroll
+        for (int I = 0; I < 4; ++I) {  // the diagonal block's values are replaced later
+          kn0[I] = __expf(fminf(gbI0[I] - G0[r], 80.f));
+          kn1[I] = __expf(fminf(gbI1[I] - G1[r], 80.f));
+        }
+      }
+      *kp = tc::pack2<BF16>(k0 * ea0, k1 * ea1);
+      *qp = tc::pack2<BF16>(q0 * ea0, q1 * ea1);
+      *reinterpret_cast<uint32_t*>(smem + kKg + kb * 8192 + off) = tc::pack2<BF16>(k0 * x0, k1 * x1);
+      *reinterpret_cast<uint32_t*>(rec + kKWsKd + kb * 8192 + off) = tc::pack2<false>(k0 * kd0, k1 * kd1);
+#pragma unroll
+      for (int I = 0; I < 4; ++I)
+        if (I >= J)
+          *reinterpret_cast<uint32_t*>(smem + kKn + kn_off(I) + kb * kn_blk(I) + off) =
+              tc::pack2<BF16>(k0 * kn0[I], k1 * kn1[I]);
+      qg0[r] = q0 * x0;
+      qg1[r] = q1 * x1;
+    }
+    // (Q . exp(G))^T rows ch, ch + 1, tokens 16 J .. 16 J + 15: two 16-byte pieces each
+#pragma unroll
+    for (int h8 = 0; h8 < 2; ++h8) {
+      const float* s0 = qg0 + 8 * h8;
+      const float* s1 = qg1 + 8 * h8;
+      *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch, 2 * J + h8)) =
+          make_uint4(tc::pack2<BF16>(s0[0], s0[1]), tc::pack2<BF16>(s0[2], s0[3]),
+                     tc::pack2<BF16>(s0[4], s0[5]), tc::pack2<BF16>(s0[6], s0[7]));
+      *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch + 1, 2 * J + h8)) =
+          make_uint4(tc::pack2<BF16>(s1[0], s1[1]), tc::pack2<BF16>(s1[2], s1[3]),
+                     tc::pack2<BF16>(s1[4], s1[5]), tc::pack2<BF16>(s1[6], s1[7]));
+    }
+    tc::fence_proxy_async();  // the scaled tiles are MMA operands
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (ok && tid == 0) {  // per row block I: [K-rows; Q-rows] x right factors of block I
+    tc::fence_after_sync();
+#pragma unroll
+    for (int I = 0; I < 4; ++I) {
+      const uint32_t idesc = tc::idesc_f16(128, 16 * (I + 1), false, false, BF16);
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        tc::mma(tmem + 8 * I * (I + 1), tc::kmajor_desc(sb + kKQ, kKQBlock, s),
+                tc::kmajor_desc(sb + kKn + kn_off(I), kn_blk(I), s), idesc, s > 0);
+    }
+    tc::commit(&bars[1]);
+  }
+  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[1], 0));
+  float* sG = reinterpret_cast<float*>(smem + kGs);
+  if (ok) {
+    tc::fence_after_sync();
+    if (!fast) {  // G table for the direct diagonal blocks (the right factors are consumed)
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        *reinterpret_cast<float2*>(sG + (16 * J + r) * kGLd + ch) = make_float2(G0[r], G1[r]);
+    }
+  }
+  __syncthreads();
+  float* AT = reinterpret_cast<float*>(smem + kAT);
+  if (ok) {
+    // ---- A and P rows.  Warp quarter q4 reads TMEM lanes 32 q4 .. (q4 < 2: A
+    // rows, else P rows); the warp pair (w, w + 4) splits its 32 rows by
+    // block: warp half hw serves the lanes of row block Iw.
+    const int q4 = warp & 3, hw = warp >> 2;
+    const bool isA = q4 < 2;
+    const int Iw = 2 * (q4 & 1) + hw;
+    const int i = 32 * (q4 & 1) + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
+    float r[64];
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb)
+      if (cb <= Iw) tc::tmem_ld16(tmem + lane_base + 8 * Iw * (Iw + 1) + cb * 16, *reinterpret_cast<float(*)[16]>(r + 16 * cb));
+    tc::tmem_wait_ld();
+    if ((lane >> 4) == hw) {
+      const int lim = isA ? i : i + 1;  // A: j < i; P: j <= i
+      float dg[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) dg[jj] = 0.f;
+      if (!fast && t0 + i < T) {  // direct diagonal block
+        const IO* src = static_cast<const IO*>(isA ? a.k : a.q);
+        const IO* krow = static_cast<const IO*>(a.k);
+        const int64_t rs = static_cast<int64_t>(a.Hqk) * kD;  // token stride
+        const int64_t base = (static_cast<int64_t>(b) * T + t0) * rs + static_cast<int64_t>(hq) * kD;
+        const uint32_t* arow = reinterpret_cast<const uint32_t*>(src + base + i * rs);
+        const float* Gi = sG + i * kGLd;
+        for (int cp = 0; cp < 64; ++cp) {
+          const uint32_t aw = __ldg(arow + cp);
+          const float a0 = tc::unpack_lo<BF16>(aw), a1 = tc::unpack_hi<BF16>(aw);
+          const float2 gi = *reinterpret_cast<const float2*>(Gi + 2 * cp);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = 16 * Iw + jj;
+            if (j < lim && t0 + j < T) {
+              const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(krow + base + j * rs) + cp);
+              const float2 gj = *reinterpret_cast<const float2*>(sG + j * kGLd + 2 * cp);
+              dg[jj] += a0 * tc::unpack_lo<BF16>(kw) * __expf(gi.x - gj.x) +
+                        a1 * tc::unpack_hi<BF16>(kw) * __expf(gi.y - gj.y);
+            }
+          }
+        }
+      }
+      auto val = [&](int j) -> float {  // j compile-time after unrolling
+        const float v = (!fast && (j >> 4) == Iw) ? dg[j & 15] : r[j];
+        return j < lim ? v : 0.f;
+      };
+      if (isA) {
+        const float bi = sBeta[i];
+#pragma unroll
+        for (int j4 = 0; j4 < 64; j4 += 4)
+          *reinterpret_cast<float4*>(AT + i * kLd + j4) =
+              make_float4(bi * val(j4), bi * val(j4 + 1), bi * val(j4 + 2), bi * val(j4 + 3));
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8)
+          tc::sts128(sb + kTu + tc::sw128_offset(i, c8), tc::pack2<BF16>(val(8 * c8), val(8 * c8 + 1)),
+                     tc::pack2<BF16>(val(8 * c8 + 2), val(8 * c8 + 3)),
+                     tc::pack2<BF16>(val(8 * c8 + 4), val(8 * c8 + 5)),
+                     tc::pack2<BF16>(val(8 * c8 + 6), val(8 * c8 + 7)));
+      }
+    }
+    tc::fence_proxy_async();  // the P tile is read by a bulk copy
+  }
+  __syncthreads();
+  if (ok && tid == 0) {
+    bulk_s2g(rec + kKWsP, smem + kTu, 8192);
+    bulk_commit();
+  }
+  if (ok && warp < 4) solve_unit_lower(AT, reinterpret_cast<float*>(smem + kMs), warp, lane, 2);
+  if (ok && tid == 0) bulk_wait_read();  // the P staging tile may be overwritten
+  __syncthreads();
+  if (ok && warp < 4) {
+    // T_u = T diag(beta): rows 16 w .. 16 w + 15; lane l the 16-byte chunk l % 8
+    // of rows 16 w + l / 8 + 4 s (four whole rows per store instruction), to
+    // the record and to the W-product operand tile
+    const int c8 = lane & 7;
+    const float4 b0 = *reinterpret_cast<const float4*>(sBeta + 8 * c8);
+    const float4 b1 = *reinterpret_cast<const float4*>(sBeta + 8 * c8 + 4);
+    const float bj[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int i = 16 * warp + (lane >> 3) + 4 * s4;
+      const float4 u0 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8);
+      const float4 u1 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8 + 4);
+      const float tv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint32_t uu[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j0 = 8 * c8 + 2 * e;
+        uu[e] = tc::pack2<BF16>((j0 <= i) ? tv[2 * e] * bj[2 * e] : 0.f,
+                                (j0 + 1 <= i) ? tv[2 * e + 1] * bj[2 * e + 1] : 0.f);
+      }
+      const uint32_t off = tc::sw128_offset(i, c8);
+      *reinterpret_cast<uint4*>(rec + kKWsTu + off) = make_uint4(uu[0], uu[1], uu[2], uu[3]);
+      tc::sts128(sb + kTu + off, uu[0], uu[1], uu[2], uu[3]);
+    }
+    tc::fence_proxy_async();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (ok && tid == 0) {  // W^T = (K . exp(G))^T T_u^T
+    tc::fence_after_sync();
+    constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, BF16);
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      tc::mma(tmem + kTmW, tc::mnmajor_desc(sb + kKg, 8192, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+    tc::commit(&bars[2]);
+  }
+  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[2], 0));
+  if (ok && warp < 4) {  // W^T rows d_k = 32 w + lane, 64 tokens, MN-major
+    tc::fence_after_sync();
+    const int k = warp * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+    for (int ih = 0; ih < 2; ++ih) {
+      float r[32];
+      tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32, *reinterpret_cast<float(*)[16]>(r));
+      tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+      tc::tmem_wait_ld();
+      store_row16_global<BF16>(rec + kKWsWT, k, ih * 4, r);
+      store_row16_global<BF16>(rec + kKWsWT, k, ih * 4 + 2, r + 16);
+    }
+  }
+  if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
+  if (tid == 0) bulk_wait_all();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
+}
+
 size_t workspace_bytes(const gdn_prefill_args_t& a) {
   const size_t nchunks = (static_cast<size_t>(a.T) + kC - 1) / kC;
   return static_cast<size_t>(a.B) * a.Hv * nchunks * kWsUnit;
@@ -1048,7 +1552,7 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   if (rc) return rc;
   if (static_cast<int>(state::kSmemAlloc) > di.smem_optin) return GDN_ERR_SHAPE;
   auto k1 = intra_kernel<BF16>;
-  auto k2 = state_kernel<BF16>;
+  auto k2 = state_kernel<BF16, false>;
   if ((rc = ensure_smem_attr(k1, intra::kSmemAlloc, attr_intra))) return rc;
   if ((rc = ensure_smem_attr(k2, state::kSmemAlloc, attr_state))) return rc;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1094,6 +1598,67 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   return GDN_OK;
 }
 
+size_t kda_workspace_bytes(const gdn_prefill_args_t& a) {
+  const size_t nchunks = (static_cast<size_t>(a.T) + kC - 1) / kC;
+  return static_cast<size_t>(a.B) * a.Hv * nchunks * kKWsUnit;
+}
+
+// KDA chunked prefill: kda_intra_kernel, then state_kernel<., true> as a
+// programmatic dependent.  Arguments validated by the caller.
+template <bool BF16>
+int launch_kda(const gdn_prefill_args_t& a, cudaStream_t stream) {
+  static std::atomic<uint64_t> attr_intra{0}, attr_state{0};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (static_cast<int>(state::kSmemAlloc) > di.smem_optin) return GDN_ERR_SHAPE;
+  auto k1 = kda_intra_kernel<BF16>;
+  auto k2 = state_kernel<BF16, true>;
+  if ((rc = ensure_smem_attr(k1, kintra::kSmemAlloc, attr_intra))) return rc;
+  if ((rc = ensure_smem_attr(k2, state::kSmemAlloc, attr_state))) return rc;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mq, mk, mv;
+  const uint32_t box[4] = {64, 1, kC, 1};
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(a.dk), static_cast<uint64_t>(a.Hqk),
+                              static_cast<uint64_t>(a.T), static_cast<uint64_t>(a.B)};
+    const uint64_t str[3] = {static_cast<uint64_t>(a.dk) * 2, static_cast<uint64_t>(a.Hqk) * a.dk * 2,
+                             static_cast<uint64_t>(a.T) * a.Hqk * a.dk * 2};
+    if ((rc = tensor_map(&mq, dt, 4, a.q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = tensor_map(&mk, dt, 4, a.k, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(a.dv), static_cast<uint64_t>(a.Hv),
+                              static_cast<uint64_t>(a.T), static_cast<uint64_t>(a.B)};
+    const uint64_t str[3] = {static_cast<uint64_t>(a.dv) * 2, static_cast<uint64_t>(a.Hv) * a.dv * 2,
+                             static_cast<uint64_t>(a.T) * a.Hv * a.dv * 2};
+    if ((rc = tensor_map(&mv, dt, 4, a.v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  }
+  Params p;
+  p.a = a;
+  p.nchunks = (a.T + kC - 1) / kC;
+  p.group = a.Hv / a.Hqk;
+  p.ws = static_cast<unsigned char*>(a.workspace);
+  const unsigned n1 = static_cast<unsigned>(a.B * a.Hv * p.nchunks);
+  k1<<<n1, kintra::kThreads, kintra::kSmemAlloc, stream>>>(p, mq, mk);
+  if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
+  cfg.blockDim = dim3(state::kThreads);
+  cfg.dynamicSmemBytes = state::kSmemAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k2, p, mq, mk, mv) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_LAUNCH;
+  }
+  return GDN_OK;
+}
+
 int validate(const gdn_prefill_args_t* a) {
   if (!a) return GDN_ERR_NULL;
   if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->final_state || !a->o) return GDN_ERR_NULL;
@@ -1113,8 +1678,27 @@ int validate(const gdn_prefill_args_t* a) {
   return GDN_OK;
 }
 
+// The chunked KDA path: d_k = d_v = 128 with a workspace (gdn_prefill
+// shapes otherwise); called by kda_prefill_launch after its own checks.
+int kda_chunked_launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
+  if (a.dk != kD || a.dv != kD) return GDN_ERR_SHAPE;
+  const int64_t nchunks = (static_cast<int64_t>(a.T) + kC - 1) / kC;
+  if (static_cast<int64_t>(a.B) * a.Hv * nchunks > 0x7FFFFFFF) return GDN_ERR_SHAPE;
+  if (!a.workspace || a.workspace_bytes < kda_workspace_bytes(a)) return GDN_ERR_WORKSPACE;
+  if (!aligned16(a.workspace) || !aligned16(a.final_state) ||
+      (a.initial_state && !aligned16(a.initial_state)))
+    return GDN_ERR_ALIGN;
+  return a.io_dtype == GDN_DT_BF16 ? launch_kda<true>(a, stream) : launch_kda<false>(a, stream);
+}
+
 }  // namespace prefill
 }  // namespace gdn
+
+extern "C" size_t kda_prefill_workspace_size(const gdn_prefill_args_t* args) {
+  if (!args || args->B < 1 || args->T < 1 || args->Hv < 1) return 0;
+  if (args->dk != gdn::prefill::kD || args->dv != gdn::prefill::kD) return 0;  // recurrent form
+  return gdn::prefill::kda_workspace_bytes(*args);
+}
 
 #ifdef GDN_PREFILL_TRACE
 extern "C" int gdn_prefill_cta_read(unsigned long long* host) {

@@ -576,12 +576,20 @@ extern "C" int kda_prefill_trace_read(unsigned long long* host) {
 }
 #endif
 
+namespace gdn {
+namespace prefill {
+int kda_chunked_launch(const gdn_prefill_args_t& a, cudaStream_t stream);  // gdn_prefill.cu
+}
+}  // namespace gdn
+
 extern "C" int kda_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream) {
   int rc = gdn::kda_prefill::validate(args);
   if (rc) return rc;
   gdn::DeviceInfo di;
   if ((rc = gdn::device_info(&di))) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  // chunked tensor-core form when the caller passes a workspace (d = 128)
+  if (args->workspace) return gdn::prefill::kda_chunked_launch(*args, s);
   return args->io_dtype == GDN_DT_BF16 ? gdn::kda_prefill::launch<__nv_bfloat16>(*args, s)
                                        : gdn::kda_prefill::launch<__half>(*args, s);
 }

@@ -289,9 +289,21 @@ int gdn_prefill_launch_noalloc(const gdn_prefill_args_t* args, gdn_stream_t stre
  * gdn_prefill_launch, except that g is the per-channel log gate
  * [B, T, Hv, d_k] (g_dtype) and chunk is ignored.  d_k, d_v in {64, 128, 256};
  * g 16-byte aligned, beta and the states 4-byte aligned.  initial_state may
- * equal final_state (updated in place).  No workspace.
+ * equal final_state (updated in place).
+ * Two forms, chosen by args->workspace:
+ *   - NULL: the recurrent form (state on chip, CUDA cores), any listed d.
+ *   - non-NULL (d_k = d_v = 128 only; >= kda_prefill_workspace_size bytes,
+ *     16-byte aligned, as are the states): the chunked tensor-core form,
+ *     64-token chunks, the per-channel decays inside the WY transform.
  */
 int kda_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
+
+/*
+ * Workspace of the chunked KDA prefill for these arguments, in bytes: one
+ * 66,048-byte record per (sequence, value head, 64-token chunk); 0 when the
+ * shapes have no chunked form (d_k or d_v other than 128).
+ */
+size_t kda_prefill_workspace_size(const gdn_prefill_args_t* args);
 
 /* ------------------------------------------------------------------------
  * Multi-GPU: all-gather of per-rank decode outputs with the copy engines.

@@ -1,6 +1,7 @@
 """GPU parity of the KDA prefill against the reference KDA step applied token
 by token (float64 oracle).  Tolerances: bf16 outputs rtol 2e-2 / atol 1e-2;
-final state max-abs 1e-3."""
+final state max-abs 1e-3.  Both forms are covered: the chunked tensor-core
+form (d = 128, the default there) and the recurrent form (every d)."""
 from __future__ import annotations
 
 import numpy as np
@@ -54,10 +55,11 @@ def test_kda_prefill_unequal_head_dims(pkg, inputs, orc, dk, dv):
     assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
 
 
-def test_kda_prefill_long_sequence(pkg, inputs, orc):
+@pytest.mark.parametrize("form", ["chunked", "recurrent"])
+def test_kda_prefill_long_sequence(pkg, inputs, orc, form):
     """T = 4096 (the prefill length of the GDN prefill config), 8 heads."""
     p = inputs.make_kda_prefill_inputs(1, 4096, 8, 8, 128, seed=4)
-    o, S = pkg.kda_prefill(*_dev(p), check=True)
+    o, S = pkg.kda_prefill(*_dev(p), form=form, check=True)
     o_ref, s_ref = orc.kda_prefill(p.q, p.k, p.v, p.g, p.beta)
     np.testing.assert_allclose(o.float().cpu().numpy(), o_ref, rtol=O_RTOL, atol=O_ATOL)
     assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
@@ -102,8 +104,9 @@ def test_kda_prefill_rejects_bad_args(pkg, inputs):
         pkg.kda_prefill(q, k, v, g[..., 0].contiguous(), beta)  # a GDN (per-head) gate
 
 
+@pytest.mark.parametrize("form", ["chunked", "recurrent"])
 @pytest.mark.parametrize("kind", ["strong", "underflow"])
-def test_kda_prefill_extreme_gates(pkg, inputs, orc, kind):
+def test_kda_prefill_extreme_gates(pkg, inputs, orc, kind, form):
     """Gates far outside the config distribution: strong decay (g down to -30
     per token) and gates whose exp() underflows to zero (g = -200).  The
     kernel's rescaled state must renormalise mid-chunk and stay finite."""
@@ -116,7 +119,46 @@ def test_kda_prefill_extreme_gates(pkg, inputs, orc, kind):
     S0 = _state(2, 2, 128)
     o_ref, s_ref = orc.kda_prefill(p.q, p.k, p.v, g, p.beta, S0.double().numpy())
     o, S = pkg.kda_prefill(p.q.to(DEV), p.k.to(DEV), p.v.to(DEV), g.to(DEV), p.beta.to(DEV),
-                           S0.to(DEV), check=True)
+                           S0.to(DEV), form=form, check=True)
     assert torch.isfinite(o.float()).all() and torch.isfinite(S).all()
     np.testing.assert_allclose(o.float().cpu().numpy(), o_ref, rtol=O_RTOL, atol=O_ATOL)
     assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
+
+
+@pytest.mark.parametrize("B,T,Hqk,Hv,init,io,gdt", [
+    (1, 64, 1, 1, False, torch.bfloat16, torch.float32),    # one whole chunk
+    (2, 100, 2, 4, True, torch.bfloat16, torch.float32),    # ragged tail, GQA 2
+    (1, 200, 1, 2, True, torch.float16, torch.bfloat16),    # f16 I/O, bf16 gate, 4 chunks
+    (1, 77, 2, 2, True, torch.bfloat16, torch.float16),     # f16 gate
+    (3, 1, 1, 1, True, torch.bfloat16, torch.float32),      # a single token
+])
+def test_kda_chunked_matches_oracle(pkg, inputs, orc, B, T, Hqk, Hv, init, io, gdt):
+    """The chunked form on its own (d = 128): ragged chunks, GQA, gate and I/O
+    dtypes, against the float64 reference recurrence."""
+    p = inputs.make_kda_prefill_inputs(B, T, Hqk, Hv, 128, seed=T + 7, io_dtype=io, g_dtype=gdt)
+    S0 = _state(B, Hv, 128) if init else None
+    o_ref, s_ref = orc.kda_prefill(p.q, p.k, p.v, p.g, p.beta,
+                                   None if S0 is None else S0.double().numpy(), scale=0.75)
+    o, S = pkg.kda_prefill(*_dev(p), None if S0 is None else S0.to(DEV), scale=0.75,
+                           form="chunked", check=True)
+    np.testing.assert_allclose(o.float().cpu().numpy(), o_ref, rtol=O_RTOL, atol=O_ATOL)
+    assert np.abs(S.cpu().numpy() - s_ref).max() < S_ATOL
+
+
+def test_kda_chunked_equals_recurrent_at_config_size(pkg, inputs):
+    """B = 4, T = 4096, H = 32 (the bench workload): the two forms agree on
+    every output and state element (the oracle would take minutes here; the
+    recurrent form is itself pinned to it above)."""
+    p = inputs.make_kda_prefill_inputs(4, 4096, 32, 32, 128, seed=3, device=DEV)
+    x = (p.q, p.k, p.v, p.g, p.beta)
+    oc, sc = pkg.kda_prefill(*x, form="chunked", check=True)
+    orr, sr = pkg.kda_prefill(*x, form="recurrent", check=True)
+    np.testing.assert_allclose(oc.float().cpu().numpy(), orr.float().cpu().numpy(),
+                               rtol=O_RTOL, atol=O_ATOL)
+    assert float((sc - sr).abs().max()) < S_ATOL
+
+
+def test_kda_chunked_rejects_other_head_dims(pkg, inputs):
+    p = inputs.make_kda_prefill_inputs(1, 16, 1, 1, 64, seed=0)
+    with pytest.raises(pkg.GDNError):
+        pkg.kda_prefill(*_dev(p), form="chunked")
