@@ -759,18 +759,28 @@ def run_extras(pkg, inputs, dev, hbm, bf16, with_cpu=True):
                                       "chunked_form_GFLOP": round(fl / 1e9, 2),
                                       "cpu_baseline": cpu.get("config3")}
     del p, fs, po
-    # KDA prefill (recurrent form, state on chip) at the config 3 length, H=32
+    # KDA prefill at the config 3 length, H=32: the chunked tensor-core form
+    # (the default at d = 128) and the recurrent form (state on chip)
     p = inputs.make_kda_prefill_inputs(4, 4096, 32, 32, D, seed=3, device=dev)
     fs = torch.empty((4, 32, D, D), dtype=torch.float32, device=dev)
     po = torch.empty((4, 4096, 32, D), dtype=torch.bfloat16, device=dev)
-    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
-    ms = _time_events(fn, reps=5, warm=2)
+    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs, form="chunked")
+    ms = _time_events(fn, reps=10)
+    fl = inputs.gdn_prefill_flops(4, 4096, 32, 32, D, 64)  # same chunked-form FLOPs, Hqk = Hv
+    tf = fl / (ms * 1e-3) / 1e12
     ex["kda_prefill_B4_T4096_H32"] = {
         "ms": round(ms, 4), "tokens_per_s": round(4 * 4096 / (ms * 1e-3), 1),
-        "head_tokens_per_s": round(4 * 32 * 4096 / (ms * 1e-3), 1),
-        "fp32_TOPs_recurrent": round(inputs.kda_recurrent_ops(4, 4096, 32, D) / (ms * 1e-3) / 1e12, 2),
+        "TFLOPs": round(tf, 1), "frac_of_bf16_peak": round(tf / bf16, 4),
+        "chunked_form_GFLOP": round(fl / 1e9, 2),
         "GBps_compulsory": round(inputs.kda_prefill_bytes(4, 4096, 32, 32, D) / (ms * 1e-3) / 1e9, 1),
-        "note": "recurrent form on CUDA cores; no tensor cores",
+        "note": "chunked form on tcgen05 (64-token chunks, per-channel decays in the operands)",
+        "cpu_baseline": cpu.get("kda_prefill")}
+    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs, form="recurrent")
+    ms = _time_events(fn, reps=5, warm=2)
+    ex["kda_prefill_recurrent_B4_T4096_H32"] = {
+        "ms": round(ms, 4), "tokens_per_s": round(4 * 4096 / (ms * 1e-3), 1),
+        "fp32_TOPs_recurrent": round(inputs.kda_recurrent_ops(4, 4096, 32, D) / (ms * 1e-3) / 1e12, 2),
+        "note": "recurrent form on CUDA cores (every d); no tensor cores",
         "cpu_baseline": cpu.get("kda_prefill")}
     del p, fs, po
     return ex
@@ -885,7 +895,8 @@ def run_kda_prefill(args, world, rank, local):
     p = inputs.make_kda_prefill_inputs(Bp, Tp, H, H, D, seed=3, device=dev)
     fs = torch.empty((Bp, H, D, D), dtype=torch.float32, device=dev)
     po = torch.empty((Bp, Tp, H, D), dtype=torch.bfloat16, device=dev)
-    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs)
+    fn = lambda: pkg.kda_prefill(p.q, p.k, p.v, p.g, p.beta, out=po, final_state=fs,
+                                 form=args.kda_form)
     for _ in range(args.warmup):
         fn()
     pkg.check_device_status(dev)
@@ -901,8 +912,9 @@ def run_kda_prefill(args, world, rank, local):
         print(json.dumps({"metric": "KDA prefill tokens/s", "value": round(Bp * Tp / (ms * 1e-3), 1),
                           "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": args.steps,
                           "warmup": args.warmup, "n_gpus": world,
-                          "fp32_TOPs_recurrent": round(
-                              inputs.kda_recurrent_ops(Bp, Tp, H, D) / (ms * 1e-3) / 1e12, 2),
+                          "form": args.kda_form,
+                          "TFLOPs_chunked_form": round(
+                              inputs.gdn_prefill_flops(Bp, Tp, H, H, D, 64) / (ms * 1e-3) / 1e12, 1),
                           "config": {"workload": f"KDA prefill B={Bp} T={Tp} H={H} d={D}"}}),
               flush=True)
 
@@ -932,6 +944,8 @@ def main():
                     help="decode (headline, configs[1]/4), prefill (config 3) or kda_prefill "
                          "(B=4, H=32, T=--seq); the last two for profiling")
     ap.add_argument("--seq", type=int, default=4096, help="kda_prefill sequence length")
+    ap.add_argument("--kda-form", default="chunked", choices=("chunked", "recurrent"),
+                    help="kda_prefill workload: the chunked tensor-core form or the recurrent form")
     ap.add_argument("--batch", type=int, default=B,
                     help="decode batch (default 1024, the headline; smaller for ncu captures)")
     args = ap.parse_args()

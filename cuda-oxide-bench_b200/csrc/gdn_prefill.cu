@@ -1138,20 +1138,19 @@ __global__ void __launch_bounds__(state::kThreads, 1)
 // KDA (per-channel log gate g[t][c]) version of the intra kernel.  With G the
 // in-chunk cumulative log gate per channel, every pairwise factor
 // exp(G_ic - G_jc) now depends on the channel, so the decays go into the MMA
-// operands instead of scaling the product.  For row block I (tokens 16 I ..
-// 16 I + 15) and the reference point r_I = G at token 16 I:
-//   A_ij / beta_i = sum_c [k_ic exp(G_ic - r_Ic)] [k_jc exp(r_Ic - G_jc)]
-// The left factor is <= 1 for every row of block I; the right one is <= 1 for
-// j < 16 I and at most exp(in-block decay) on the diagonal block.  One MMA per
-// row block I (N = 16 (I + 1) columns, M = 128 rows [K-rows; Q-rows]) gives
-// the A and P rows of that block.  The remaining operands of the state pass
-// (W^T, (Q . exp(G))^T, the decayed keys K . exp(G_C - G) and exp(G_C)) are
-// formed here too, so the state kernel's per-chunk work is the GDN one.
-// Fast path (every |G| <= 80 in the chunk): two exponentials per element,
-// exp(G) and exp(-G), and products of per-channel block constants.  Otherwise
-// every factor is its own exponential of a non-positive argument, and the
-// diagonal blocks of A and P are summed directly from the gates (the
-// factored form could overflow there).
+// operands instead of scaling the product:
+//   A_ij / beta_i = sum_c [k_ic exp(G_ic - r_c)] [k_jc exp(r_c - G_jc)]
+// for any reference point r.  Fast path (every |G| <= 80 in the chunk): r = 0,
+// so the left factors are K . exp(G) and Q . exp(G) — the operands the W
+// product and the state pass need anyway — and one M = 128, N = 64 MMA gives
+// all A and P rows; every factor lies in [exp(-80), exp(80)], finite in bf16.
+// Slow path (stronger decays): per row block I (tokens 16 I .. 16 I + 15)
+// r = G at token 16 I, which keeps the left factors <= 1 and the right ones
+// <= 1 below the diagonal block; one MMA per row block (N = 16 (I + 1)), and
+// the diagonal blocks, where the factored form could overflow, summed
+// directly from the gates.  The remaining operands of the state pass (W^T,
+// (Q . exp(G))^T, the decayed keys K . exp(G_C - G) and exp(G_C)) are formed
+// here too, so the state kernel's per-chunk work is the GDN one.
 namespace kintra {
 constexpr int kThreads = 256;
 constexpr uint32_t kKQ = 0;            // [K | Q] per d_k block (2 x 16 KB), scaled in place
@@ -1172,9 +1171,15 @@ constexpr uint32_t kSmemBytes = kBars + 64;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmCols = 256;      // A/P products at 8 I (I + 1) (160 columns), W^T at 192
 constexpr uint32_t kTmW = 192;
+constexpr uint32_t kTmFast = 96;       // fast path: the one 64-column product (row block 3's columns)
+constexpr uint32_t kATFast = kKn;      // fast path: A -> T and the solver scratch over the
+                                       // consumed right factors, then the Q^T staging tile
+constexpr uint32_t kQTStage = kKn + 24576;
 __host__ __device__ constexpr uint32_t kn_off(int I) { return 2048u * I * (I + 1); }
 __host__ __device__ constexpr uint32_t kn_blk(int I) { return 2048u * (I + 1); }
 static_assert(kMs + 4608 <= kKn && 64 * kGLd * 4 <= kKnBytes && kn_off(4) == kKnBytes, "smem map");
+static_assert(kATFast + kMs + 4608 <= kQTStage && kQTStage + 16384 <= kKn + kKnBytes &&
+              kQTStage % 1024 == 0, "fast-path smem map");
 }  // namespace kintra
 
 template <bool BF16>
@@ -1296,104 +1301,105 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   const bool fast = !__syncthreads_or(!in_range);  // also publishes sGb / sBeta
 
   // ---- scaled operands
+  // Fast path: one reference point for the whole chunk,
+  //   A/P = [K . exp(G); Q . exp(G)] (K . exp(-G))^T,
+  // with every factor in [exp(-80), exp(80)] (finite in bf16); the scaled K
+  // and Q are written over the raw tiles and serve the W product and the
+  // state pass as well.  Slow path: per-row-block reference points (above).
+  // The scaled tiles are bf16 for either I/O type (f16 has no room for
+  // exp(80)); what goes to the workspace is converted to the I/O type.
   bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], 0));
   if (ok) {
     const float2 gc = *reinterpret_cast<const float2*>(sGb + 4 * 128 + ch);
-    float gbI0[4], gbI1[4];
-#pragma unroll
-    for (int I = 0; I < 4; ++I) {
-      const float2 v = *reinterpret_cast<const float2*>(sGb + I * 128 + ch);
-      gbI0[I] = v.x;
-      gbI1[I] = v.y;
-    }
-    // fast-path constants: exp(-r_J), exp(G_C), exp(r_I)
-    float yb0 = 0.f, yb1 = 0.f, xc0 = 0.f, xc1 = 0.f, xb0[4] = {}, xb1[4] = {};
+    const float xc0 = expf(gc.x), xc1 = expf(gc.y);  // the state's per-chunk decay: full accuracy
+    if (J == 3) *reinterpret_cast<float2*>(rec + kKWsVec + ch * 4) = make_float2(xc0, xc1);
     if (fast) {
-      yb0 = __expf(-gbI0[J]);
-      yb1 = __expf(-gbI1[J]);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int i = 16 * J + r;
+        const uint32_t off = tc::sw128_offset(i, lane >> 2) + (lane & 3) * 4;
+        uint32_t* kp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + off);
+        uint32_t* qp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + 8192 + off);
+        const uint32_t kw = *kp, qw = *qp;
+        const float k0 = tc::unpack_lo<BF16>(kw), k1 = tc::unpack_hi<BF16>(kw);
+        const float q0 = tc::unpack_lo<BF16>(qw), q1 = tc::unpack_hi<BF16>(qw);
+        const float x0 = __expf(G0[r]), x1 = __expf(G1[r]);
+        const float n0 = k0 * __expf(-G0[r]), n1 = k1 * __expf(-G1[r]);
+        *kp = tc::pack2<true>(k0 * x0, k1 * x1);
+        *qp = tc::pack2<true>(q0 * x0, q1 * x1);
+        *reinterpret_cast<uint32_t*>(smem + kKn + kn_off(3) + kb * kn_blk(3) + off) = tc::pack2<true>(n0, n1);
+        *reinterpret_cast<uint32_t*>(rec + kKWsKd + kb * 8192 + off) = tc::pack2<false>(n0 * xc0, n1 * xc1);
+      }
+    } else {
+      float gbI0[4], gbI1[4];
 #pragma unroll
       for (int I = 0; I < 4; ++I) {
-        xb0[I] = __expf(gbI0[I]);
-        xb1[I] = __expf(gbI1[I]);
+        const float2 v = *reinterpret_cast<const float2*>(sGb + I * 128 + ch);
+        gbI0[I] = v.x;
+        gbI1[I] = v.y;
       }
-    }
-    xc0 = expf(gc.x);  // the state's per-chunk decay: full-accuracy exponential
-    xc1 = expf(gc.y);
-    if (J == 3) *reinterpret_cast<float2*>(rec + kKWsVec + ch * 4) = make_float2(xc0, xc1);
-    float qg0[16], qg1[16];
+      float qg0[16], qg1[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int i = 16 * J + r;
-      const uint32_t off = tc::sw128_offset(i, lane >> 2) + (lane & 3) * 4;
-      uint32_t* kp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + off);
-      uint32_t* qp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + 8192 + off);
-      const uint32_t kw = *kp, qw = *qp;
-      const float k0 = tc::unpack_lo<BF16>(kw), k1 = tc::unpack_hi<BF16>(kw);
-      const float q0 = tc::unpack_lo<BF16>(qw), q1 = tc::unpack_hi<BF16>(qw);
-      float x0, x1, ea0, ea1, kd0, kd1, kn0[4], kn1[4];
-      if (fast) {
-        x0 = __expf(G0[r]);
-        x1 = __expf(G1[r]);
-        const float y0 = __expf(-G0[r]), y1 = __expf(-G1[r]);
-        ea0 = x0 * yb0;
-        ea1 = x1 * yb1;
-        kd0 = y0 * xc0;
-        kd1 = y1 * xc1;
+      for (int r = 0; r < 16; ++r) {
+        const int i = 16 * J + r;
+        const uint32_t off = tc::sw128_offset(i, lane >> 2) + (lane & 3) * 4;
+        uint32_t* kp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + off);
+        uint32_t* qp = reinterpret_cast<uint32_t*>(smem + kKQ + kb * kKQBlock + 8192 + off);
+        const uint32_t kw = *kp, qw = *qp;
+        const float k0 = tc::unpack_lo<BF16>(kw), k1 = tc::unpack_hi<BF16>(kw);
+        const float q0 = tc::unpack_lo<BF16>(qw), q1 = tc::unpack_hi<BF16>(qw);
+        // every factor an exponential of a non-positive argument (the
+        // diagonal block's right factors are clamped and replaced later)
+        const float x0 = __expf(G0[r]), x1 = __expf(G1[r]);
+        const float ea0 = __expf(G0[r] - gbI0[J]), ea1 = __expf(G1[r] - gbI1[J]);
+        const float kd0 = __expf(gc.x - G0[r]), kd1 = __expf(gc.y - G1[r]);
+        *kp = tc::pack2<true>(k0 * ea0, k1 * ea1);
+        *qp = tc::pack2<true>(q0 * ea0, q1 * ea1);
+        *reinterpret_cast<uint32_t*>(smem + kKg + kb * 8192 + off) = tc::pack2<true>(k0 * x0, k1 * x1);
+        *reinterpret_cast<uint32_t*>(rec + kKWsKd + kb * 8192 + off) = tc::pack2<false>(k0 * kd0, k1 * kd1);
 #pragma unroll
-        for (int I = 0; I < 4; ++I) {
-          kn0[I] = y0 * xb0[I];
-          kn1[I] = y1 * xb1[I];
-        }
-      } else {
-        x0 = __expf(G0[r]);
-        x1 = __expf(G1[r]);
-        ea0 = __expf(G0[r] - gbI0[J]);
-        ea1 = __expf(G1[r] - gbI1[J]);
-        kd0 = __expf(gc.x - G0[r]);
-        kd1 = __expf(gc.y - G1[r]);
-#pragma unroll
-        for (int I = 0; I < 4; ++I) {  // the diagonal block's values are replaced later
-          kn0[I] = __expf(fminf(gbI0[I] - G0[r], 80.f));
-          kn1[I] = __expf(fminf(gbI1[I] - G1[r], 80.f));
-        }
+        for (int I = 0; I < 4; ++I)
+          if (I >= J)
+            *reinterpret_cast<uint32_t*>(smem + kKn + kn_off(I) + kb * kn_blk(I) + off) =
+                tc::pack2<true>(k0 * __expf(fminf(gbI0[I] - G0[r], 80.f)),
+                                k1 * __expf(fminf(gbI1[I] - G1[r], 80.f)));
+        qg0[r] = q0 * x0;
+        qg1[r] = q1 * x1;
       }
-      *kp = tc::pack2<BF16>(k0 * ea0, k1 * ea1);
-      *qp = tc::pack2<BF16>(q0 * ea0, q1 * ea1);
-      *reinterpret_cast<uint32_t*>(smem + kKg + kb * 8192 + off) = tc::pack2<BF16>(k0 * x0, k1 * x1);
-      *reinterpret_cast<uint32_t*>(rec + kKWsKd + kb * 8192 + off) = tc::pack2<false>(k0 * kd0, k1 * kd1);
+      // (Q . exp(G))^T rows ch, ch + 1, tokens 16 J .. 16 J + 15: two 16-byte pieces each
 #pragma unroll
-      for (int I = 0; I < 4; ++I)
-        if (I >= J)
-          *reinterpret_cast<uint32_t*>(smem + kKn + kn_off(I) + kb * kn_blk(I) + off) =
-              tc::pack2<BF16>(k0 * kn0[I], k1 * kn1[I]);
-      qg0[r] = q0 * x0;
-      qg1[r] = q1 * x1;
-    }
-    // (Q . exp(G))^T rows ch, ch + 1, tokens 16 J .. 16 J + 15: two 16-byte pieces each
-#pragma unroll
-    for (int h8 = 0; h8 < 2; ++h8) {
-      const float* s0 = qg0 + 8 * h8;
-      const float* s1 = qg1 + 8 * h8;
-      *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch, 2 * J + h8)) =
-          make_uint4(tc::pack2<BF16>(s0[0], s0[1]), tc::pack2<BF16>(s0[2], s0[3]),
-                     tc::pack2<BF16>(s0[4], s0[5]), tc::pack2<BF16>(s0[6], s0[7]));
-      *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch + 1, 2 * J + h8)) =
-          make_uint4(tc::pack2<BF16>(s1[0], s1[1]), tc::pack2<BF16>(s1[2], s1[3]),
-                     tc::pack2<BF16>(s1[4], s1[5]), tc::pack2<BF16>(s1[6], s1[7]));
+      for (int h8 = 0; h8 < 2; ++h8) {
+        const float* s0 = qg0 + 8 * h8;
+        const float* s1 = qg1 + 8 * h8;
+        *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch, 2 * J + h8)) =
+            make_uint4(tc::pack2<BF16>(s0[0], s0[1]), tc::pack2<BF16>(s0[2], s0[3]),
+                       tc::pack2<BF16>(s0[4], s0[5]), tc::pack2<BF16>(s0[6], s0[7]));
+        *reinterpret_cast<uint4*>(rec + kKWsQT + tc::sw128_offset(ch + 1, 2 * J + h8)) =
+            make_uint4(tc::pack2<BF16>(s1[0], s1[1]), tc::pack2<BF16>(s1[2], s1[3]),
+                       tc::pack2<BF16>(s1[4], s1[5]), tc::pack2<BF16>(s1[6], s1[7]));
+      }
     }
     tc::fence_proxy_async();  // the scaled tiles are MMA operands
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (ok && tid == 0) {  // per row block I: [K-rows; Q-rows] x right factors of block I
+  if (ok && tid == 0) {
     tc::fence_after_sync();
-#pragma unroll
-    for (int I = 0; I < 4; ++I) {
-      const uint32_t idesc = tc::idesc_f16(128, 16 * (I + 1), false, false, BF16);
+    if (fast) {  // one N = 64 product into the columns of row block 3
+      constexpr uint32_t idesc = tc::idesc_f16(128, 64, false, false, true);
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        tc::mma(tmem + 8 * I * (I + 1), tc::kmajor_desc(sb + kKQ, kKQBlock, s),
-                tc::kmajor_desc(sb + kKn + kn_off(I), kn_blk(I), s), idesc, s > 0);
+        tc::mma(tmem + kTmFast, tc::kmajor_desc(sb + kKQ, kKQBlock, s),
+                tc::kmajor_desc(sb + kKn + kn_off(3), kn_blk(3), s), idesc, s > 0);
+    } else {  // per row block I: [K-rows; Q-rows] x right factors of block I
+#pragma unroll
+      for (int I = 0; I < 4; ++I) {
+        const uint32_t idesc = tc::idesc_f16(128, 16 * (I + 1), false, false, true);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          tc::mma(tmem + 8 * I * (I + 1), tc::kmajor_desc(sb + kKQ, kKQBlock, s),
+                  tc::kmajor_desc(sb + kKn + kn_off(I), kn_blk(I), s), idesc, s > 0);
+      }
     }
     tc::commit(&bars[1]);
   }
@@ -1408,66 +1414,95 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     }
   }
   __syncthreads();
-  float* AT = reinterpret_cast<float*>(smem + kAT);
+  // A -> T: over the consumed right factors (fast path: the scaled K / Q tiles
+  // are still needed) or over the K / Q tiles (slow path)
+  float* AT = reinterpret_cast<float*>(smem + (fast ? kATFast : kAT));
+  float* Ms = AT + 64 * kLd;
+  const int q4 = warp & 3, hw = warp >> 2;
+  const uint32_t lane_q = static_cast<uint32_t>(q4 * 32) << 16;
   if (ok) {
     // ---- A and P rows.  Warp quarter q4 reads TMEM lanes 32 q4 .. (q4 < 2: A
-    // rows, else P rows); the warp pair (w, w + 4) splits its 32 rows by
-    // block: warp half hw serves the lanes of row block Iw.
-    const int q4 = warp & 3, hw = warp >> 2;
+    // rows, else P rows) and the warp pair (w, w + 4) splits the work.
     const bool isA = q4 < 2;
-    const int Iw = 2 * (q4 & 1) + hw;
     const int i = 32 * (q4 & 1) + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
-    float r[64];
-#pragma unroll
-    for (int cb = 0; cb < 4; ++cb)
-      if (cb <= Iw) tc::tmem_ld16(tmem + lane_base + 8 * Iw * (Iw + 1) + cb * 16, *reinterpret_cast<float(*)[16]>(r + 16 * cb));
-    tc::tmem_wait_ld();
-    if ((lane >> 4) == hw) {
-      const int lim = isA ? i : i + 1;  // A: j < i; P: j <= i
-      float dg[16];
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) dg[jj] = 0.f;
-      if (!fast && t0 + i < T) {  // direct diagonal block
-        const IO* src = static_cast<const IO*>(isA ? a.k : a.q);
-        const IO* krow = static_cast<const IO*>(a.k);
-        const int64_t rs = static_cast<int64_t>(a.Hqk) * kD;  // token stride
-        const int64_t base = (static_cast<int64_t>(b) * T + t0) * rs + static_cast<int64_t>(hq) * kD;
-        const uint32_t* arow = reinterpret_cast<const uint32_t*>(src + base + i * rs);
-        const float* Gi = sG + i * kGLd;
-        for (int cp = 0; cp < 64; ++cp) {
-          const uint32_t aw = __ldg(arow + cp);
-          const float a0 = tc::unpack_lo<BF16>(aw), a1 = tc::unpack_hi<BF16>(aw);
-          const float2 gi = *reinterpret_cast<const float2*>(Gi + 2 * cp);
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = 16 * Iw + jj;
-            if (j < lim && t0 + j < T) {
-              const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(krow + base + j * rs) + cp);
-              const float2 gj = *reinterpret_cast<const float2*>(sG + j * kGLd + 2 * cp);
-              dg[jj] += a0 * tc::unpack_lo<BF16>(kw) * __expf(gi.x - gj.x) +
-                        a1 * tc::unpack_hi<BF16>(kw) * __expf(gi.y - gj.y);
-            }
-          }
-        }
-      }
-      auto val = [&](int j) -> float {  // j compile-time after unrolling
-        const float v = (!fast && (j >> 4) == Iw) ? dg[j & 15] : r[j];
-        return j < lim ? v : 0.f;
-      };
+    const int lim = isA ? i : i + 1;  // A: j < i; P: j <= i
+    if (fast) {  // warp half hw: columns 32 hw .. 32 hw + 31
+      float r[32];
+      tc::tmem_ld16(tmem + lane_q + kTmFast + 32 * hw, *reinterpret_cast<float(*)[16]>(r));
+      tc::tmem_ld16(tmem + lane_q + kTmFast + 32 * hw + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+      tc::tmem_wait_ld();
       if (isA) {
         const float bi = sBeta[i];
 #pragma unroll
-        for (int j4 = 0; j4 < 64; j4 += 4)
-          *reinterpret_cast<float4*>(AT + i * kLd + j4) =
-              make_float4(bi * val(j4), bi * val(j4 + 1), bi * val(j4 + 2), bi * val(j4 + 3));
+        for (int j4 = 0; j4 < 32; j4 += 4) {
+          const int j = 32 * hw + j4;
+          *reinterpret_cast<float4*>(AT + i * kLd + j) =
+              make_float4(j < lim ? bi * r[j4] : 0.f, j + 1 < lim ? bi * r[j4 + 1] : 0.f,
+                          j + 2 < lim ? bi * r[j4 + 2] : 0.f, j + 3 < lim ? bi * r[j4 + 3] : 0.f);
+        }
       } else {
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8)
-          tc::sts128(sb + kTu + tc::sw128_offset(i, c8), tc::pack2<BF16>(val(8 * c8), val(8 * c8 + 1)),
-                     tc::pack2<BF16>(val(8 * c8 + 2), val(8 * c8 + 3)),
-                     tc::pack2<BF16>(val(8 * c8 + 4), val(8 * c8 + 5)),
-                     tc::pack2<BF16>(val(8 * c8 + 6), val(8 * c8 + 7)));
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = (32 * hw + 8 * c8 + e < lim) ? r[8 * c8 + e] : 0.f;
+          tc::sts128(sb + kTu + tc::sw128_offset(i, 4 * hw + c8), tc::pack2<BF16>(v[0], v[1]),
+                     tc::pack2<BF16>(v[2], v[3]), tc::pack2<BF16>(v[4], v[5]), tc::pack2<BF16>(v[6], v[7]));
+        }
+      }
+    } else {  // the warp half hw serves the lanes of row block Iw
+      const int Iw = 2 * (q4 & 1) + hw;
+      float r[64];
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb)
+        if (cb <= Iw)
+          tc::tmem_ld16(tmem + lane_q + 8 * Iw * (Iw + 1) + cb * 16, *reinterpret_cast<float(*)[16]>(r + 16 * cb));
+      tc::tmem_wait_ld();
+      if ((lane >> 4) == hw) {
+        float dg[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) dg[jj] = 0.f;
+        if (t0 + i < T) {  // direct diagonal block
+          const IO* src = static_cast<const IO*>(isA ? a.k : a.q);
+          const IO* krow = static_cast<const IO*>(a.k);
+          const int64_t rs = static_cast<int64_t>(a.Hqk) * kD;  // token stride
+          const int64_t base = (static_cast<int64_t>(b) * T + t0) * rs + static_cast<int64_t>(hq) * kD;
+          const uint32_t* arow = reinterpret_cast<const uint32_t*>(src + base + i * rs);
+          const float* Gi = sG + i * kGLd;
+          for (int cp = 0; cp < 64; ++cp) {
+            const uint32_t aw = __ldg(arow + cp);
+            const float a0 = tc::unpack_lo<BF16>(aw), a1 = tc::unpack_hi<BF16>(aw);
+            const float2 gi = *reinterpret_cast<const float2*>(Gi + 2 * cp);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = 16 * Iw + jj;
+              if (j < lim && t0 + j < T) {
+                const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(krow + base + j * rs) + cp);
+                const float2 gj = *reinterpret_cast<const float2*>(sG + j * kGLd + 2 * cp);
+                dg[jj] += a0 * tc::unpack_lo<BF16>(kw) * __expf(gi.x - gj.x) +
+                          a1 * tc::unpack_hi<BF16>(kw) * __expf(gi.y - gj.y);
+              }
+            }
+          }
+        }
+        auto val = [&](int j) -> float {  // j compile-time after unrolling
+          const float v = ((j >> 4) == Iw) ? dg[j & 15] : r[j];
+          return j < lim ? v : 0.f;
+        };
+        if (isA) {
+          const float bi = sBeta[i];
+#pragma unroll
+          for (int j4 = 0; j4 < 64; j4 += 4)
+            *reinterpret_cast<float4*>(AT + i * kLd + j4) =
+                make_float4(bi * val(j4), bi * val(j4 + 1), bi * val(j4 + 2), bi * val(j4 + 3));
+        } else {
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8)
+            tc::sts128(sb + kTu + tc::sw128_offset(i, c8), tc::pack2<BF16>(val(8 * c8), val(8 * c8 + 1)),
+                       tc::pack2<BF16>(val(8 * c8 + 2), val(8 * c8 + 3)),
+                       tc::pack2<BF16>(val(8 * c8 + 4), val(8 * c8 + 5)),
+                       tc::pack2<BF16>(val(8 * c8 + 6), val(8 * c8 + 7)));
+        }
       }
     }
     tc::fence_proxy_async();  // the P tile is read by a bulk copy
@@ -1477,13 +1512,42 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     bulk_s2g(rec + kKWsP, smem + kTu, 8192);
     bulk_commit();
   }
-  if (ok && warp < 4) solve_unit_lower(AT, reinterpret_cast<float*>(smem + kMs), warp, lane, 2);
+  if (ok && warp < 4) solve_unit_lower(AT, Ms, warp, lane, 2);
+  if (ok && fast && warp >= 4) {
+    // meanwhile: (Q . exp(G))^T, MN-major rows d_k, from the scaled Q tile by
+    // 8 x 8 transposes; warp w - 4 takes d_k rows 32 (w - 4) .. + 31
+    const int w = warp - 4, m = lane >> 3, r8 = lane & 7;
+    const uint32_t qsrc = sb + kKQ + 8192;
+    const uint32_t qt = sb + kQTStage;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kc = w * 4 + j;  // d_k rows 8 kc .. 8 kc + 7
+      const uint32_t src = qsrc + (kc >> 3) * kKQBlock;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t v[4];
+        tc::ldsm_x4_trans(src + tc::sw128_offset(8 * (4 * hh + m) + r8, kc & 7), v);
+        if (!BF16) {  // bf16 tile -> f16 workspace
+#pragma unroll
+          for (int mm = 0; mm < 4; ++mm)
+            v[mm] = tc::pack2<false>(tc::unpack_lo<true>(v[mm]), tc::unpack_hi<true>(v[mm]));
+        }
+        tc::stsm_x4(qt + tc::sw128_offset(8 * kc + r8, 4 * hh + m), v);
+      }
+    }
+    tc::fence_proxy_async();
+    tc::group_sync(3, 128);
+    if (tid == 128) {
+      bulk_s2g(rec + kKWsQT, smem + kQTStage, 16384);
+      bulk_commit();
+    }
+  }
   if (ok && tid == 0) bulk_wait_read();  // the P staging tile may be overwritten
   __syncthreads();
   if (ok && warp < 4) {
     // T_u = T diag(beta): rows 16 w .. 16 w + 15; lane l the 16-byte chunk l % 8
     // of rows 16 w + l / 8 + 4 s (four whole rows per store instruction), to
-    // the record and to the W-product operand tile
+    // the record (I/O type) and to the W-product operand tile (bf16)
     const int c8 = lane & 7;
     const float4 b0 = *reinterpret_cast<const float4*>(sBeta + 8 * c8);
     const float4 b1 = *reinterpret_cast<const float4*>(sBeta + 8 * c8 + 4);
@@ -1494,16 +1558,18 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
       const float4 u0 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8);
       const float4 u1 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8 + 4);
       const float tv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      uint32_t uu[4];
+      uint32_t uu[4], ub[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int j0 = 8 * c8 + 2 * e;
-        uu[e] = tc::pack2<BF16>((j0 <= i) ? tv[2 * e] * bj[2 * e] : 0.f,
-                                (j0 + 1 <= i) ? tv[2 * e + 1] * bj[2 * e + 1] : 0.f);
+        const float v0 = (j0 <= i) ? tv[2 * e] * bj[2 * e] : 0.f;
+        const float v1 = (j0 + 1 <= i) ? tv[2 * e + 1] * bj[2 * e + 1] : 0.f;
+        uu[e] = tc::pack2<BF16>(v0, v1);
+        ub[e] = BF16 ? uu[e] : tc::pack2<true>(v0, v1);
       }
       const uint32_t off = tc::sw128_offset(i, c8);
       *reinterpret_cast<uint4*>(rec + kKWsTu + off) = make_uint4(uu[0], uu[1], uu[2], uu[3]);
-      tc::sts128(sb + kTu + off, uu[0], uu[1], uu[2], uu[3]);
+      tc::sts128(sb + kTu + off, ub[0], ub[1], ub[2], ub[3]);
     }
     tc::fence_proxy_async();
   }
@@ -1511,29 +1577,26 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   __syncthreads();
   if (ok && tid == 0) {  // W^T = (K . exp(G))^T T_u^T
     tc::fence_after_sync();
-    constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, BF16);
+    constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, true);
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      tc::mma(tmem + kTmW, tc::mnmajor_desc(sb + kKg, 8192, s), tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+      tc::mma(tmem + kTmW, fast ? tc::mnmajor_desc(sb + kKQ, kKQBlock, s) : tc::mnmajor_desc(sb + kKg, 8192, s),
+              tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
     tc::commit(&bars[2]);
   }
   if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[2], 0));
-  if (ok && warp < 4) {  // W^T rows d_k = 32 w + lane, 64 tokens, MN-major
+  if (ok) {  // W^T rows d_k = 32 q4 + lane, tokens 32 hw .. 32 hw + 31, MN-major
     tc::fence_after_sync();
-    const int k = warp * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-#pragma unroll
-    for (int ih = 0; ih < 2; ++ih) {
-      float r[32];
-      tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32, *reinterpret_cast<float(*)[16]>(r));
-      tc::tmem_ld16(tmem + lane_base + kTmW + ih * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
-      tc::tmem_wait_ld();
-      store_row16_global<BF16>(rec + kKWsWT, k, ih * 4, r);
-      store_row16_global<BF16>(rec + kKWsWT, k, ih * 4 + 2, r + 16);
-    }
+    const int k = q4 * 32 + lane;
+    float r[32];
+    tc::tmem_ld16(tmem + lane_q + kTmW + hw * 32, *reinterpret_cast<float(*)[16]>(r));
+    tc::tmem_ld16(tmem + lane_q + kTmW + hw * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+    tc::tmem_wait_ld();
+    store_row16_global<BF16>(rec + kKWsWT, k, hw * 4, r);
+    store_row16_global<BF16>(rec + kKWsWT, k, hw * 4 + 2, r + 16);
   }
   if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
-  if (tid == 0) bulk_wait_all();
+  if (tid == 0 || tid == 128) bulk_wait_all();
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
