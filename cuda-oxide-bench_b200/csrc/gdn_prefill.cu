@@ -70,7 +70,16 @@ __device__ unsigned long long g_cta[8192 * 5];  // start, end (globaltimer), smi
   do {                                                                                   \
     if (blockIdx.x < 4096 && threadIdx.x == 0) g_trace1[blockIdx.x * 8 + (ph)] = global_timer_ns(); \
   } while (0)
+// per-CTA phase clocks of the KDA intra kernel (SM cycles)
+__device__ unsigned long long g_ktrace[4096 * 16];
+#define KTRACE(ph)                                                                          \
+  do {                                                                                      \
+    if (blockIdx.x < 4096 && threadIdx.x == 0) g_ktrace[blockIdx.x * 16 + (ph)] = clock64(); \
+  } while (0)
 #else
+#define KTRACE(ph) \
+  do {             \
+  } while (0)
 #define TRACE1(ph) \
   do {             \
   } while (0)
@@ -1161,6 +1170,7 @@ constexpr uint32_t kKn = 32768;        // right factors of row block I: 16 (I + 
 constexpr uint32_t kKnBytes = 40960;
 constexpr int kGLd = 130;              // slow path: G [64][kGLd] fp32 over the right factors
 constexpr uint32_t kGs = kKn;
+constexpr uint32_t kGTile = kKn;       // the raw gate tile (up to 32 KB), consumed before the build
 constexpr uint32_t kKg = kKn + kKnBytes;  // 73728: K . exp(G), 2 d_k blocks x 8 KB
 constexpr uint32_t kTu = kKg + 16384;     // 90112: P staging, then T_u
 constexpr uint32_t kBeta = kTu + 8192;    // 98304: beta[64]
@@ -1185,7 +1195,7 @@ static_assert(kATFast + kMs + 4608 <= kQTStage && kQTStage + 16384 <= kKn + kKnB
 template <bool BF16>
 __global__ void __launch_bounds__(kintra::kThreads, 2)
     kda_intra_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
-                     const __grid_constant__ CUtensorMap map_k) {
+                     const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_g) {
   using namespace kintra;
   using IO = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ unsigned char smem_raw[];
@@ -1206,26 +1216,28 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   const int J = warp >> 1, kb = warp & 1;
   const int ch = kb * 64 + 2 * lane;
 
+  KTRACE(0);
   pdl_wait();
   pdl_launch_dependents();
   // raw gates of this thread's 16 tokens and 2 channels (converted at first use)
-  uint32_t gr0[16], gr1[16];
+  auto load_gates = [&](uint32_t (&g0)[16], uint32_t (&g1)[16]) {
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    gr0[r] = 0u;  // padded tokens: no decay
-    gr1[r] = 0u;
-    const int t = t0 + 16 * J + r;
-    if (t < T) {
-      const int64_t gi = ((static_cast<int64_t>(b) * T + t) * a.Hv + h) * kD + ch;
-      if (a.g_dtype == GDN_DT_F32) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.g) + (gi >> 1));
-        gr0[r] = u.x;
-        gr1[r] = u.y;
-      } else {
-        gr0[r] = __ldg(reinterpret_cast<const uint32_t*>(a.g) + (gi >> 1));
+    for (int r = 0; r < 16; ++r) {
+      g0[r] = 0u;  // padded tokens: no decay
+      g1[r] = 0u;
+      const int t = t0 + 16 * J + r;
+      if (t < T) {
+        const int64_t gi = ((static_cast<int64_t>(b) * T + t) * a.Hv + h) * kD + ch;
+        if (a.g_dtype == GDN_DT_F32) {
+          const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.g) + (gi >> 1));
+          g0[r] = u.x;
+          g1[r] = u.y;
+        } else {
+          g0[r] = __ldg(reinterpret_cast<const uint32_t*>(a.g) + (gi >> 1));
+        }
       }
     }
-  }
+  };
   uint32_t braw = 0u;
   if (tid < kC && t0 + tid < T) {
     const int64_t bi = (static_cast<int64_t>(b) * T + t0 + tid) * a.Hv + h;
@@ -1248,32 +1260,65 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[0], 4 * 8192);
+  const bool gf32 = a.g_dtype == GDN_DT_F32;
+  if (tid == 0) {  // K, Q tiles and the gate tile [64 tokens][128 channels] (zero past T)
+    mbar_arrive_expect_tx(&bars[0], 4 * 8192 + kC * kD * (gf32 ? 4 : 2));
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
       unsigned char* kq = smem + kKQ + blk * kKQBlock;
       tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
       tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
     }
+    tc::tma_load_4d(smem + kGTile, &map_g, 0, h, t0, b, &bars[0]);
+  }
+  KTRACE(11);
+  bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], 0));
+  KTRACE(12);
+  uint32_t gr0[16], gr1[16];  // raw gates of this thread's tokens and channels
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const int i = 16 * J + r;
+    if (gf32) {
+      const uint2 u = *reinterpret_cast<const uint2*>(smem + kGTile + (i * kD + ch) * 4);
+      gr0[r] = u.x;
+      gr1[r] = u.y;
+    } else {
+      gr0[r] = *reinterpret_cast<const uint32_t*>(smem + kGTile + (i * kD + ch) * 2);
+      gr1[r] = 0u;
+    }
   }
 
-  // ---- in-chunk cumulative log gate per channel (while K / Q are in flight)
+  // ---- in-chunk cumulative log gate per channel
   float* sBeta = reinterpret_cast<float*>(smem + kBeta);
   float* sGb = reinterpret_cast<float*>(smem + kGb);
   float* sPart = reinterpret_cast<float*>(smem + kPart);
-  float G0[16], G1[16];
-  {
+  // in-block inclusive prefix sums of the raw gates (channels ch, ch + 1)
+  auto block_scan = [&](const uint32_t (&g0)[16], const uint32_t (&g1)[16], float (&o0)[16], float (&o1)[16]) {
     float run0 = 0.f, run1 = 0.f;
     const bool f32 = a.g_dtype == GDN_DT_F32;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      run0 += gate(gr0[r], false);
-      run1 += f32 ? gate(gr1[r], false) : gate(gr0[r], true);
-      G0[r] = run0;
-      G1[r] = run1;
+      run0 += gate(g0[r], false);
+      run1 += f32 ? gate(g1[r], false) : gate(g0[r], true);
+      o0[r] = run0;
+      o1[r] = run1;
     }
-    *reinterpret_cast<float2*>(sPart + J * 128 + ch) = make_float2(run0, run1);
+  };
+  // G of the earlier blocks of the chunk (from the block sums in sPart)
+  auto block_offset = [&](float& o0, float& o1) {
+    o0 = 0.f;
+    o1 = 0.f;
+    for (int jb = 0; jb < J; ++jb) {
+      const float2 pp = *reinterpret_cast<const float2*>(sPart + jb * 128 + ch);
+      o0 += pp.x;
+      o1 += pp.y;
+    }
+  };
+  float G0[16], G1[16];
+  {
+    block_scan(gr0, gr1, G0, G1);
+    *reinterpret_cast<float2*>(sPart + J * 128 + ch) = make_float2(G0[15], G1[15]);
+    KTRACE(13);
     if (tid < kC) {
       sBeta[tid] = a.beta_dtype == GDN_DT_F32   ? __uint_as_float(braw)
                    : a.beta_dtype == GDN_DT_BF16 ? __uint_as_float(braw << 16)
@@ -1283,12 +1328,8 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   __syncthreads();
   bool in_range = true;
   {
-    float o0 = 0.f, o1 = 0.f;
-    for (int jb = 0; jb < J; ++jb) {
-      const float2 pp = *reinterpret_cast<const float2*>(sPart + jb * 128 + ch);
-      o0 += pp.x;
-      o1 += pp.y;
-    }
+    float o0, o1;
+    block_offset(o0, o1);
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       G0[r] += o0;
@@ -1299,6 +1340,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     if (J == 3) *reinterpret_cast<float2*>(sGb + 4 * 128 + ch) = make_float2(G0[15], G1[15]);
   }
   const bool fast = !__syncthreads_or(!in_range);  // also publishes sGb / sBeta
+  KTRACE(1);
 
   // ---- scaled operands
   // Fast path: one reference point for the whole chunk,
@@ -1308,7 +1350,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   // state pass as well.  Slow path: per-row-block reference points (above).
   // The scaled tiles are bf16 for either I/O type (f16 has no room for
   // exp(80)); what goes to the workspace is converted to the I/O type.
-  bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], 0));
+  KTRACE(2);
   if (ok) {
     const float2 gc = *reinterpret_cast<const float2*>(sGb + 4 * 128 + ch);
     const float xc0 = expf(gc.x), xc1 = expf(gc.y);  // the state's per-chunk decay: full accuracy
@@ -1403,14 +1445,22 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     }
     tc::commit(&bars[1]);
   }
+  KTRACE(3);
   if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[1], 0));
+  KTRACE(4);
   float* sG = reinterpret_cast<float*>(smem + kGs);
   if (ok) {
     tc::fence_after_sync();
-    if (!fast) {  // G table for the direct diagonal blocks (the right factors are consumed)
+    if (!fast) {  // G table for the direct diagonal blocks (the right factors are consumed),
+                  // recomputed from the gates so that G need not stay in registers
+      uint32_t h0[16], h1[16];
+      float F0[16], F1[16], o0, o1;
+      load_gates(h0, h1);
+      block_scan(h0, h1, F0, F1);
+      block_offset(o0, o1);
 #pragma unroll
       for (int r = 0; r < 16; ++r)
-        *reinterpret_cast<float2*>(sG + (16 * J + r) * kGLd + ch) = make_float2(G0[r], G1[r]);
+        *reinterpret_cast<float2*>(sG + (16 * J + r) * kGLd + ch) = make_float2(F0[r] + o0, F1[r] + o1);
     }
   }
   __syncthreads();
@@ -1508,6 +1558,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     tc::fence_proxy_async();  // the P tile is read by a bulk copy
   }
   __syncthreads();
+  KTRACE(5);
   if (ok && tid == 0) {
     bulk_s2g(rec + kKWsP, smem + kTu, 8192);
     bulk_commit();
@@ -1552,11 +1603,17 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     const float4 b0 = *reinterpret_cast<const float4*>(sBeta + 8 * c8);
     const float4 b1 = *reinterpret_cast<const float4*>(sBeta + 8 * c8 + 4);
     const float bj[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float4 ua[4], ub4[4];  // loads first (the stores below would order them)
 #pragma unroll
     for (int s4 = 0; s4 < 4; ++s4) {
       const int i = 16 * warp + (lane >> 3) + 4 * s4;
-      const float4 u0 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8);
-      const float4 u1 = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8 + 4);
+      ua[s4] = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8);
+      ub4[s4] = *reinterpret_cast<const float4*>(AT + i * kLd + 8 * c8 + 4);
+    }
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int i = 16 * warp + (lane >> 3) + 4 * s4;
+      const float4 u0 = ua[s4], u1 = ub4[s4];
       const float tv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint32_t uu[4], ub[4];
 #pragma unroll
@@ -1575,6 +1632,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   }
   tc::fence_before_sync();
   __syncthreads();
+  KTRACE(7);
   if (ok && tid == 0) {  // W^T = (K . exp(G))^T T_u^T
     tc::fence_after_sync();
     constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, true);
@@ -1595,10 +1653,12 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     store_row16_global<BF16>(rec + kKWsWT, k, hw * 4, r);
     store_row16_global<BF16>(rec + kKWsWT, k, hw * 4 + 2, r + 16);
   }
+  KTRACE(8);
   if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
   if (tid == 0 || tid == 128) bulk_wait_all();
   tc::fence_before_sync();
   __syncthreads();
+  KTRACE(9);
   if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
 }
 
@@ -1697,13 +1757,26 @@ int launch_kda(const gdn_prefill_args_t& a, cudaStream_t stream) {
                              static_cast<uint64_t>(a.T) * a.Hv * a.dv * 2};
     if ((rc = tensor_map(&mv, dt, 4, a.v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   }
+  CUtensorMap mg;  // per-channel gates [B, T, Hv, d_k], one chunk x all channels per box
+  {
+    const uint64_t es = a.g_dtype == GDN_DT_F32 ? 4 : 2;
+    const CUtensorMapDataType gdt = a.g_dtype == GDN_DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : a.g_dtype == GDN_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t dims[4] = {static_cast<uint64_t>(a.dk), static_cast<uint64_t>(a.Hv),
+                              static_cast<uint64_t>(a.T), static_cast<uint64_t>(a.B)};
+    const uint64_t str[3] = {a.dk * es, static_cast<uint64_t>(a.Hv) * a.dk * es,
+                             static_cast<uint64_t>(a.T) * a.Hv * a.dk * es};
+    const uint32_t gbox[4] = {static_cast<uint32_t>(kD), 1, kC, 1};
+    if ((rc = tensor_map(&mg, gdt, 4, a.g, dims, str, gbox, CU_TENSOR_MAP_SWIZZLE_NONE))) return rc;
+  }
   Params p;
   p.a = a;
   p.nchunks = (a.T + kC - 1) / kC;
   p.group = a.Hv / a.Hqk;
   p.ws = static_cast<unsigned char*>(a.workspace);
   const unsigned n1 = static_cast<unsigned>(a.B * a.Hv * p.nchunks);
-  k1<<<n1, kintra::kThreads, kintra::kSmemAlloc, stream>>>(p, mq, mk);
+  k1<<<n1, kintra::kThreads, kintra::kSmemAlloc, stream>>>(p, mq, mk, mg);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
@@ -1772,6 +1845,9 @@ extern "C" int gdn_prefill_trace1_read(unsigned long long* host) {
                  cudaSuccess
              ? 0
              : 1;
+}
+extern "C" int kda_intra_trace_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, gdn::prefill::g_ktrace, sizeof(gdn::prefill::g_ktrace)) == cudaSuccess ? 0 : 1;
 }
 extern "C" int gdn_prefill_trace_read(unsigned long long* host) {
   return cudaMemcpyFromSymbol(host, gdn::prefill::g_trace, sizeof(gdn::prefill::g_trace)) ==
