@@ -40,6 +40,7 @@
 // leaving its loop.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -116,6 +117,8 @@ struct Params {
   int32_t nchunks;
   int32_t group;
   unsigned char* ws;
+  uint32_t* slow_count;  // KDA: units deferred to the slow-path kernel, and their list
+  int32_t* slow_list;
 };
 
 template <bool BF16>
@@ -1185,6 +1188,17 @@ constexpr uint32_t kTmFast = 96;       // fast path: the one 64-column product (
 constexpr uint32_t kATFast = kKn;      // fast path: A -> T and the solver scratch over the
                                        // consumed right factors, then the Q^T staging tile
 constexpr uint32_t kQTStage = kKn + 24576;
+// compact fast-path-only map (kda_intra_fast): [K | Q] 32 KB, then R (32 KB):
+// the raw gate tile, then K . exp(-G), then A -> T and the solver scratch;
+// P staging / T_u at the end of R; the vectors; the barriers
+constexpr uint32_t kFoR = 32768;
+constexpr uint32_t kFoTu = kFoR + 23552;
+constexpr uint32_t kFoVec = 65536;
+constexpr uint32_t kFoBars = kFoVec + 256 + 5 * 128 * 4 + 4 * 128 * 4;
+constexpr uint32_t kFoSmemAlloc = kFoBars + 64 + 1024;
+constexpr uint32_t kFoTmCols = 128;    // the A/P product at 0, W^T at 64
+static_assert(kFoR + 64 * kLd * 4 + 4608 <= kFoTu && kFoTu + 8192 <= kFoVec && kFoTu % 1024 == 0,
+              "compact smem map");
 __host__ __device__ constexpr uint32_t kn_off(int I) { return 2048u * I * (I + 1); }
 __host__ __device__ constexpr uint32_t kn_blk(int I) { return 2048u * (I + 1); }
 static_assert(kMs + 4608 <= kKn && 64 * kGLd * 4 <= kKnBytes && kn_off(4) == kKnBytes, "smem map");
@@ -1192,23 +1206,23 @@ static_assert(kATFast + kMs + 4608 <= kQTStage && kQTStage + 16384 <= kKn + kKnB
               kQTStage % 1024 == 0, "fast-path smem map");
 }  // namespace kintra
 
-template <bool BF16>
-__global__ void __launch_bounds__(kintra::kThreads, 2)
-    kda_intra_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
-                     const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_g) {
+// One (batch, value head, chunk) unit of the KDA intra kernel.  FO selects the
+// compact fast-path-only variant (three CTAs per SM); it returns false, having
+// written nothing, for a chunk whose |G| exceeds the fast path's range.  The
+// other variant (FO = false) runs the slow path for such chunks.  `par` is the
+// mbarrier phase of this unit (units of one CTA alternate).
+template <bool BF16, bool FO>
+__device__ __forceinline__ bool kda_unit(const Params& p, const CUtensorMap& map_q, const CUtensorMap& map_k,
+                                         const CUtensorMap& map_g, int unit, uint32_t par,
+                                         unsigned char* smem, uint64_t* bars, uint32_t tmem) {
   using namespace kintra;
   using IO = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);  // [0] TMA, [1] A/P MMA, [2] W MMA
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3);
   const gdn_prefill_args_t& a = p.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int per_c = a.B * a.Hv;
-  const int c = p.nchunks - 1 - static_cast<int>(blockIdx.x) / per_c;
-  const int bh = static_cast<int>(blockIdx.x) % per_c;
+  const int c = p.nchunks - 1 - unit / per_c;
+  const int bh = unit % per_c;
   const int b = bh / a.Hv, h = bh % a.Hv, hq = h / p.group;
   const int T = a.T, t0 = c * kC;
   unsigned char* rec = p.ws + (static_cast<size_t>(bh) * p.nchunks + c) * kKWsUnit;
@@ -1217,8 +1231,15 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   const int ch = kb * 64 + 2 * lane;
 
   KTRACE(0);
-  pdl_wait();
-  pdl_launch_dependents();
+  // smem map of this kernel variant (FO: the compact fast-path-only map)
+  constexpr uint32_t oGT = FO ? kFoR : kGTile;          // raw gate tile
+  constexpr uint32_t oKnF = FO ? kFoR : kKn + kn_off(3);  // fast path: K . exp(-G), d_k block stride 8 KB
+  constexpr uint32_t oATF = FO ? kFoR : kATFast;        // fast path: A -> T, then the solver scratch
+  constexpr uint32_t oTu = FO ? kFoTu : kTu;            // P staging, then T_u
+  constexpr uint32_t oBeta = FO ? kFoVec : kBeta;
+  constexpr uint32_t oGb = oBeta + 256, oPart = oGb + 5 * 128 * 4;
+  constexpr uint32_t oTmFast = FO ? 0 : kTmFast, oTmW = FO ? 64 : kTmW;
+  static_assert(kn_blk(3) == 8192, "fast right-factor tile: 64 rows per d_k block");
   // raw gates of this thread's 16 tokens and 2 channels (converted at first use)
   auto load_gates = [&](uint32_t (&g0)[16], uint32_t (&g1)[16]) {
 #pragma unroll
@@ -1251,15 +1272,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
   };
 
-  if (warp == 0) tc::tmem_alloc(tmem_holder, kTmCols);
-  if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
-    fence_mbar_init();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_holder;
+  __syncthreads();  // the previous unit of this CTA is done with shared memory
   const bool gf32 = a.g_dtype == GDN_DT_F32;
   if (tid == 0) {  // K, Q tiles and the gate tile [64 tokens][128 channels] (zero past T)
     mbar_arrive_expect_tx(&bars[0], 4 * 8192 + kC * kD * (gf32 ? 4 : 2));
@@ -1269,29 +1282,29 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
       tc::tma_load_4d(kq, &map_k, blk * 64, hq, t0, b, &bars[0]);
       tc::tma_load_4d(kq + 8192, &map_q, blk * 64, hq, t0, b, &bars[0]);
     }
-    tc::tma_load_4d(smem + kGTile, &map_g, 0, h, t0, b, &bars[0]);
+    tc::tma_load_4d(smem + oGT, &map_g, 0, h, t0, b, &bars[0]);
   }
   KTRACE(11);
-  bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], 0));
+  bool ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[0], par));
   KTRACE(12);
   uint32_t gr0[16], gr1[16];  // raw gates of this thread's tokens and channels
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     const int i = 16 * J + r;
     if (gf32) {
-      const uint2 u = *reinterpret_cast<const uint2*>(smem + kGTile + (i * kD + ch) * 4);
+      const uint2 u = *reinterpret_cast<const uint2*>(smem + oGT + (i * kD + ch) * 4);
       gr0[r] = u.x;
       gr1[r] = u.y;
     } else {
-      gr0[r] = *reinterpret_cast<const uint32_t*>(smem + kGTile + (i * kD + ch) * 2);
+      gr0[r] = *reinterpret_cast<const uint32_t*>(smem + oGT + (i * kD + ch) * 2);
       gr1[r] = 0u;
     }
   }
 
   // ---- in-chunk cumulative log gate per channel
-  float* sBeta = reinterpret_cast<float*>(smem + kBeta);
-  float* sGb = reinterpret_cast<float*>(smem + kGb);
-  float* sPart = reinterpret_cast<float*>(smem + kPart);
+  float* sBeta = reinterpret_cast<float*>(smem + oBeta);
+  float* sGb = reinterpret_cast<float*>(smem + oGb);
+  float* sPart = reinterpret_cast<float*>(smem + oPart);
   // in-block inclusive prefix sums of the raw gates (channels ch, ch + 1)
   auto block_scan = [&](const uint32_t (&g0)[16], const uint32_t (&g1)[16], float (&o0)[16], float (&o1)[16]) {
     float run0 = 0.f, run1 = 0.f;
@@ -1339,7 +1352,14 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     *reinterpret_cast<float2*>(sGb + J * 128 + ch) = make_float2(G0[0], G1[0]);
     if (J == 3) *reinterpret_cast<float2*>(sGb + 4 * 128 + ch) = make_float2(G0[15], G1[15]);
   }
-  const bool fast = !__syncthreads_or(!in_range);  // also publishes sGb / sBeta
+  // also publishes sGb / sBeta.  The compact variant defers a chunk outside
+  // the fast path's range to the other variant, which runs only the slow path.
+  if (FO) {
+    if (__syncthreads_or(ok && !in_range)) return false;
+  } else {
+    __syncthreads();
+  }
+  constexpr bool fast = FO;
   KTRACE(1);
 
   // ---- scaled operands
@@ -1369,7 +1389,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
         const float n0 = k0 * __expf(-G0[r]), n1 = k1 * __expf(-G1[r]);
         *kp = tc::pack2<true>(k0 * x0, k1 * x1);
         *qp = tc::pack2<true>(q0 * x0, q1 * x1);
-        *reinterpret_cast<uint32_t*>(smem + kKn + kn_off(3) + kb * kn_blk(3) + off) = tc::pack2<true>(n0, n1);
+        *reinterpret_cast<uint32_t*>(smem + oKnF + kb * 8192 + off) = tc::pack2<true>(n0, n1);
         *reinterpret_cast<uint32_t*>(rec + kKWsKd + kb * 8192 + off) = tc::pack2<false>(n0 * xc0, n1 * xc1);
       }
     } else {
@@ -1431,8 +1451,8 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
       constexpr uint32_t idesc = tc::idesc_f16(128, 64, false, false, true);
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        tc::mma(tmem + kTmFast, tc::kmajor_desc(sb + kKQ, kKQBlock, s),
-                tc::kmajor_desc(sb + kKn + kn_off(3), kn_blk(3), s), idesc, s > 0);
+        tc::mma(tmem + oTmFast, tc::kmajor_desc(sb + kKQ, kKQBlock, s),
+                tc::kmajor_desc(sb + oKnF, 8192, s), idesc, s > 0);
     } else {  // per row block I: [K-rows; Q-rows] x right factors of block I
 #pragma unroll
       for (int I = 0; I < 4; ++I) {
@@ -1446,7 +1466,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     tc::commit(&bars[1]);
   }
   KTRACE(3);
-  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[1], 0));
+  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[1], par));
   KTRACE(4);
   float* sG = reinterpret_cast<float*>(smem + kGs);
   if (ok) {
@@ -1466,7 +1486,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   __syncthreads();
   // A -> T: over the consumed right factors (fast path: the scaled K / Q tiles
   // are still needed) or over the K / Q tiles (slow path)
-  float* AT = reinterpret_cast<float*>(smem + (fast ? kATFast : kAT));
+  float* AT = reinterpret_cast<float*>(smem + (fast ? oATF : kAT));
   float* Ms = AT + 64 * kLd;
   const int q4 = warp & 3, hw = warp >> 2;
   const uint32_t lane_q = static_cast<uint32_t>(q4 * 32) << 16;
@@ -1478,8 +1498,8 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     const int lim = isA ? i : i + 1;  // A: j < i; P: j <= i
     if (fast) {  // warp half hw: columns 32 hw .. 32 hw + 31
       float r[32];
-      tc::tmem_ld16(tmem + lane_q + kTmFast + 32 * hw, *reinterpret_cast<float(*)[16]>(r));
-      tc::tmem_ld16(tmem + lane_q + kTmFast + 32 * hw + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+      tc::tmem_ld16(tmem + lane_q + oTmFast + 32 * hw, *reinterpret_cast<float(*)[16]>(r));
+      tc::tmem_ld16(tmem + lane_q + oTmFast + 32 * hw + 16, *reinterpret_cast<float(*)[16]>(r + 16));
       tc::tmem_wait_ld();
       if (isA) {
         const float bi = sBeta[i];
@@ -1496,7 +1516,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
           float v[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] = (32 * hw + 8 * c8 + e < lim) ? r[8 * c8 + e] : 0.f;
-          tc::sts128(sb + kTu + tc::sw128_offset(i, 4 * hw + c8), tc::pack2<BF16>(v[0], v[1]),
+          tc::sts128(sb + oTu + tc::sw128_offset(i, 4 * hw + c8), tc::pack2<BF16>(v[0], v[1]),
                      tc::pack2<BF16>(v[2], v[3]), tc::pack2<BF16>(v[4], v[5]), tc::pack2<BF16>(v[6], v[7]));
         }
       }
@@ -1548,7 +1568,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
         } else {
 #pragma unroll
           for (int c8 = 0; c8 < 8; ++c8)
-            tc::sts128(sb + kTu + tc::sw128_offset(i, c8), tc::pack2<BF16>(val(8 * c8), val(8 * c8 + 1)),
+            tc::sts128(sb + oTu + tc::sw128_offset(i, c8), tc::pack2<BF16>(val(8 * c8), val(8 * c8 + 1)),
                        tc::pack2<BF16>(val(8 * c8 + 2), val(8 * c8 + 3)),
                        tc::pack2<BF16>(val(8 * c8 + 4), val(8 * c8 + 5)),
                        tc::pack2<BF16>(val(8 * c8 + 6), val(8 * c8 + 7)));
@@ -1560,16 +1580,17 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
   __syncthreads();
   KTRACE(5);
   if (ok && tid == 0) {
-    bulk_s2g(rec + kKWsP, smem + kTu, 8192);
+    bulk_s2g(rec + kKWsP, smem + oTu, 8192);
     bulk_commit();
   }
   if (ok && warp < 4) solve_unit_lower(AT, Ms, warp, lane, 2);
   if (ok && fast && warp >= 4) {
     // meanwhile: (Q . exp(G))^T, MN-major rows d_k, from the scaled Q tile by
-    // 8 x 8 transposes; warp w - 4 takes d_k rows 32 (w - 4) .. + 31
+    // 8 x 8 transposes written straight to the record; warp w - 4 takes d_k
+    // rows 32 (w - 4) .. + 31.  Lane t holds, for transposed block mm, row
+    // t / 4 and the column pair 2 (t % 4) of that 8 x 8 block.
     const int w = warp - 4, m = lane >> 3, r8 = lane & 7;
     const uint32_t qsrc = sb + kKQ + 8192;
-    const uint32_t qt = sb + kQTStage;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int kc = w * 4 + j;  // d_k rows 8 kc .. 8 kc + 7
@@ -1578,19 +1599,13 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t v[4];
         tc::ldsm_x4_trans(src + tc::sw128_offset(8 * (4 * hh + m) + r8, kc & 7), v);
-        if (!BF16) {  // bf16 tile -> f16 workspace
 #pragma unroll
-          for (int mm = 0; mm < 4; ++mm)
-            v[mm] = tc::pack2<false>(tc::unpack_lo<true>(v[mm]), tc::unpack_hi<true>(v[mm]));
+        for (int mm = 0; mm < 4; ++mm) {
+          const uint32_t x = BF16 ? v[mm] : tc::pack2<false>(tc::unpack_lo<true>(v[mm]), tc::unpack_hi<true>(v[mm]));
+          *reinterpret_cast<uint32_t*>(rec + kKWsQT + tc::sw128_offset(8 * kc + (lane >> 2), 4 * hh + mm) +
+                                       4 * (lane & 3)) = x;
         }
-        tc::stsm_x4(qt + tc::sw128_offset(8 * kc + r8, 4 * hh + m), v);
       }
-    }
-    tc::fence_proxy_async();
-    tc::group_sync(3, 128);
-    if (tid == 128) {
-      bulk_s2g(rec + kKWsQT, smem + kQTStage, 16384);
-      bulk_commit();
     }
   }
   if (ok && tid == 0) bulk_wait_read();  // the P staging tile may be overwritten
@@ -1626,7 +1641,7 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
       }
       const uint32_t off = tc::sw128_offset(i, c8);
       *reinterpret_cast<uint4*>(rec + kKWsTu + off) = make_uint4(uu[0], uu[1], uu[2], uu[3]);
-      tc::sts128(sb + kTu + off, ub[0], ub[1], ub[2], ub[3]);
+      tc::sts128(sb + oTu + off, ub[0], ub[1], ub[2], ub[3]);
     }
     tc::fence_proxy_async();
   }
@@ -1638,28 +1653,96 @@ __global__ void __launch_bounds__(kintra::kThreads, 2)
     constexpr uint32_t kIdW = tc::idesc_f16(128, 64, true, false, true);
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      tc::mma(tmem + kTmW, fast ? tc::mnmajor_desc(sb + kKQ, kKQBlock, s) : tc::mnmajor_desc(sb + kKg, 8192, s),
-              tc::kmajor_desc(sb + kTu, 0, s), kIdW, s > 0);
+      tc::mma(tmem + oTmW, fast ? tc::mnmajor_desc(sb + kKQ, kKQBlock, s) : tc::mnmajor_desc(sb + kKg, 8192, s),
+              tc::kmajor_desc(sb + oTu, 0, s), kIdW, s > 0);
     tc::commit(&bars[2]);
   }
-  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[2], 0));
+  if (ok) ok = !named_barrier_or(1, kThreads, (lane == 0) && !mbar_wait_bounded(&bars[2], par));
   if (ok) {  // W^T rows d_k = 32 q4 + lane, tokens 32 hw .. 32 hw + 31, MN-major
     tc::fence_after_sync();
     const int k = q4 * 32 + lane;
     float r[32];
-    tc::tmem_ld16(tmem + lane_q + kTmW + hw * 32, *reinterpret_cast<float(*)[16]>(r));
-    tc::tmem_ld16(tmem + lane_q + kTmW + hw * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
+    tc::tmem_ld16(tmem + lane_q + oTmW + hw * 32, *reinterpret_cast<float(*)[16]>(r));
+    tc::tmem_ld16(tmem + lane_q + oTmW + hw * 32 + 16, *reinterpret_cast<float(*)[16]>(r + 16));
     tc::tmem_wait_ld();
     store_row16_global<BF16>(rec + kKWsWT, k, hw * 4, r);
     store_row16_global<BF16>(rec + kKWsWT, k, hw * 4 + 2, r + 16);
   }
   KTRACE(8);
   if (!ok && tid == 0) report(a.status, GDN_DEVERR_MMA_TIMEOUT);
-  if (tid == 0 || tid == 128) bulk_wait_all();
+  if (tid == 0) bulk_wait_all();  // the P tile has left shared memory
   tc::fence_before_sync();
   __syncthreads();
   KTRACE(9);
-  if (warp == 0) tc::tmem_dealloc(tmem, kTmCols);
+  tc::fence_proxy_async();  // generic writes before the next unit's TMA into the same bytes
+  return true;
+}
+
+// Fast-path kernel: one CTA per unit, three per SM.  Units outside the fast
+// path's range go to a device list for kda_intra_slow.
+template <bool BF16>
+__global__ void __launch_bounds__(kintra::kThreads, 3)
+    kda_intra_fast(const Params p, const __grid_constant__ CUtensorMap map_q,
+                   const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_g) {
+  using namespace kintra;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFoBars);  // [0] TMA, [1] A/P MMA, [2] W MMA
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3);
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x < 32) tc::tmem_alloc(tmem_holder, kFoTmCols);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const int unit = static_cast<int>(blockIdx.x);
+  if (!kda_unit<BF16, true>(p, map_q, map_k, map_g, unit, 0, smem, bars, tmem) && threadIdx.x == 0)
+    p.slow_list[atomicAdd(p.slow_count, 1u)] = unit;
+  tc::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) tc::tmem_dealloc(tmem, kFoTmCols);
+}
+
+// Slow-path kernel: a persistent grid over the units kda_intra_fast deferred
+// (usually none; it then exits at once).
+template <bool BF16>
+__global__ void __launch_bounds__(kintra::kThreads, 2)
+    kda_intra_slow(const Params p, const __grid_constant__ CUtensorMap map_q,
+                   const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_g) {
+  using namespace kintra;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3);
+  pdl_wait();  // the list is complete
+  const int n = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.slow_count));
+  if (static_cast<int>(blockIdx.x) >= n) {
+    pdl_launch_dependents();
+    return;
+  }
+  if (threadIdx.x < 32) tc::tmem_alloc(tmem_holder, kTmCols);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  uint32_t par = 0;
+  for (int i = static_cast<int>(blockIdx.x); i < n; i += static_cast<int>(gridDim.x), par ^= 1u)
+    kda_unit<BF16, false>(p, map_q, map_k, map_g, p.slow_list[i], par, smem, bars, tmem);
+  pdl_launch_dependents();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) tc::tmem_dealloc(tmem, kTmCols);
 }
 
 size_t workspace_bytes(const gdn_prefill_args_t& a) {
@@ -1701,6 +1784,8 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   p.nchunks = (a.T + kC - 1) / kC;
   p.group = a.Hv / a.Hqk;
   p.ws = static_cast<unsigned char*>(a.workspace);
+  p.slow_count = nullptr;
+  p.slow_list = nullptr;
   const unsigned n1 = static_cast<unsigned>(a.B * a.Hqk * p.nchunks);
   k1<<<n1, intra::kThreads, intra::kSmemAlloc, stream>>>(p, mq, mk);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
@@ -1721,23 +1806,32 @@ int launch(const gdn_prefill_args_t& a, cudaStream_t stream) {
   return GDN_OK;
 }
 
-size_t kda_workspace_bytes(const gdn_prefill_args_t& a) {
+// KDA workspace: the records, then the count (16 bytes) and the list of
+// units deferred to the slow-path kernel.
+size_t kda_records_bytes(const gdn_prefill_args_t& a) {
   const size_t nchunks = (static_cast<size_t>(a.T) + kC - 1) / kC;
   return static_cast<size_t>(a.B) * a.Hv * nchunks * kKWsUnit;
 }
+size_t kda_workspace_bytes(const gdn_prefill_args_t& a) {
+  const size_t units = kda_records_bytes(a) / kKWsUnit;
+  return kda_records_bytes(a) + 16 + ((units * 4 + 15) & ~size_t(15));
+}
 
-// KDA chunked prefill: kda_intra_kernel, then state_kernel<., true> as a
-// programmatic dependent.  Arguments validated by the caller.
+// KDA chunked prefill: the deferred-unit count cleared, kda_intra_fast, then
+// kda_intra_slow and state_kernel<., true> as programmatic dependents.
+// Arguments validated by the caller.
 template <bool BF16>
 int launch_kda(const gdn_prefill_args_t& a, cudaStream_t stream) {
-  static std::atomic<uint64_t> attr_intra{0}, attr_state{0};
+  static std::atomic<uint64_t> attr_fast{0}, attr_slow{0}, attr_state{0};
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
   if (static_cast<int>(state::kSmemAlloc) > di.smem_optin) return GDN_ERR_SHAPE;
-  auto k1 = kda_intra_kernel<BF16>;
+  auto k1 = kda_intra_fast<BF16>;
+  auto k1s = kda_intra_slow<BF16>;
   auto k2 = state_kernel<BF16, true>;
-  if ((rc = ensure_smem_attr(k1, kintra::kSmemAlloc, attr_intra))) return rc;
+  if ((rc = ensure_smem_attr(k1, kintra::kFoSmemAlloc, attr_fast))) return rc;
+  if ((rc = ensure_smem_attr(k1s, kintra::kSmemAlloc, attr_slow))) return rc;
   if ((rc = ensure_smem_attr(k2, state::kSmemAlloc, attr_state))) return rc;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
@@ -1775,17 +1869,31 @@ int launch_kda(const gdn_prefill_args_t& a, cudaStream_t stream) {
   p.nchunks = (a.T + kC - 1) / kC;
   p.group = a.Hv / a.Hqk;
   p.ws = static_cast<unsigned char*>(a.workspace);
+  p.slow_count = reinterpret_cast<uint32_t*>(p.ws + kda_records_bytes(a));
+  p.slow_list = reinterpret_cast<int32_t*>(p.ws + kda_records_bytes(a) + 16);
   const unsigned n1 = static_cast<unsigned>(a.B * a.Hv * p.nchunks);
-  k1<<<n1, kintra::kThreads, kintra::kSmemAlloc, stream>>>(p, mq, mk, mg);
+  if (cudaMemsetAsync(p.slow_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GDN_ERR_LAUNCH;
+  k1<<<n1, kintra::kThreads, kintra::kFoSmemAlloc, stream>>>(p, mq, mk, mg);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cs = {};
+  cs.gridDim = dim3(std::min(n1, static_cast<unsigned>(2 * di.sm_count)));
+  cs.blockDim = dim3(kintra::kThreads);
+  cs.dynamicSmemBytes = kintra::kSmemAlloc;
+  cs.stream = stream;
+  cs.attrs = attr;
+  cs.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cs, k1s, p, mq, mk, mg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_LAUNCH;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
   cfg.blockDim = dim3(state::kThreads);
   cfg.dynamicSmemBytes = state::kSmemAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, k2, p, mq, mk, mv) != cudaSuccess) {

@@ -300,8 +300,10 @@ int kda_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
 /*
  * Workspace of the chunked KDA prefill for these arguments, in bytes: one
- * 66,048-byte record per (sequence, value head, 64-token chunk); 0 when the
- * shapes have no chunked form (d_k or d_v other than 128).
+ * 66,048-byte record per (sequence, value head, 64-token chunk), plus a
+ * 16-byte count and 4 bytes per chunk for the list of chunks whose decays
+ * need the slow path; 0 when the shapes have no chunked form (d_k or d_v
+ * other than 128).
  */
 size_t kda_prefill_workspace_size(const gdn_prefill_args_t* args);
 
