@@ -684,6 +684,9 @@ __device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
   return tc::pack2<BF16>(lo, hi);
 }
 
+// dS from one f16 V'' operand (K as f16) instead of bf16 hi + lo halves
+constexpr bool kDsSingle = true;
+
 template <bool BF16, bool KDA>
 __global__ void __launch_bounds__(state::kThreads, 1)
     state_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
@@ -737,7 +740,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
   constexpr uint32_t kIdOIneg = tc::idesc_f16(128, 64, false, false, BF16, true);
   // KDA: dS^T = V'^T (K . exp(G_C - G)) takes f16 operands (the decayed keys
   // keep 11 mantissa bits; V' enters as f16 hi + lo)
-  constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, KDA ? false : BF16);
+  constexpr uint32_t kIdDS = tc::idesc_f16(128, 128, false, true, (KDA || kDsSingle) ? false : BF16);
 
   // GDN: K, Q (TMA), P and vectors (bulk) of chunk n into slot n % 3.
   // KDA: the decayed keys (in the K tile places), P and exp(G_C), all bulk.
@@ -854,6 +857,21 @@ __global__ void __launch_bounds__(state::kThreads, 1)
       if (!group_wait(&bars[kBarHMma], c & 1, kBarW, kGroupThreads)) { ok = false; break; }
       tc::fence_after_sync();
       if (tid == 0 && c + 1 < nchunks) issue_twu(c + 1);  // V / T_w / T_u slot is free again
+      if (kDsSingle && BF16) {
+        // the W product has read the K tile; dS reads it as f16 (bf16 -> f16 is
+        // exact for |k| >= 2^-14; below that it becomes subnormal)
+        unsigned char* kt = smem + kKQ + (c % 3) * kKQSlot;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const int idx = v * kGroupThreads + tid;  // 16-byte piece of the 2 x 8 KB K tile
+          uint4* pp = reinterpret_cast<uint4*>(kt + (idx >> 9) * kKQBlock + (idx & 511) * 16);
+          uint4 x = *pp;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&x);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) w[e] = tc::pack2<false>(tc::unpack_lo<true>(w[e]), tc::unpack_hi<true>(w[e]));
+          *pp = x;
+        }
+      }
       TRACE(c, 1);
 #pragma unroll
       for (int ih = 0; ih < 2; ++ih) {  // W^T -> bf16 tile, MN-major rows d_k, tokens [32 ih, +32)
@@ -1055,7 +1073,10 @@ __global__ void __launch_bounds__(state::kThreads, 1)
               const int e = q4 * 2 + e2;
               const float u0 = u[cb * 16 + 2 * e], u1 = u[cb * 16 + 2 * e + 1];
               wp[e] = tc::pack2<BF16>(u0, u1);
-              if constexpr (KDA) {  // the decay sits in the keys; V' as f16 hi + lo
+              if constexpr (kDsSingle) {  // one f16 operand: V' (KDA) or V'' (GDN)
+                wh[e] = KDA ? tc::pack2<false>(u0, u1) : tc::pack2<false>(u0 * dd[2 * e2], u1 * dd[2 * e2 + 1]);
+                wl[e] = 0u;
+              } else if constexpr (KDA) {  // the decay sits in the keys; V' as f16 hi + lo
                 const uint32_t hw = tc::pack2<false>(u0, u1);
                 wh[e] = hw;
                 wl[e] = tc::pack2<false>(u0 - tc::unpack_lo<false>(hw), u1 - tc::unpack_hi<false>(hw));
@@ -1074,7 +1095,7 @@ __global__ void __launch_bounds__(state::kThreads, 1)
                        wp[4 * k2 + 2], wp[4 * k2 + 3]);
           // this thread's V' columns were loaded (tcgen05.wait::ld) before the overwrite
           tc::tmem_st8(tmu + lane_base + half * 32 + cb * 8, wh);
-          tc::tmem_st8(tmu + lane_base + half * 32 + 16 + cb * 8, wl);
+          if (!kDsSingle) tc::tmem_st8(tmu + lane_base + half * 32 + 16 + cb * 8, wl);
         }
         tc::tmem_wait_st();
       }
@@ -1090,10 +1111,12 @@ __global__ void __launch_bounds__(state::kThreads, 1)
           for (int s = 0; s < 4; ++s)  // tokens [16 s, 16 s + 16): hi of half s / 2
             tc::mma_tmem_a(tmem + kTmDS, tmu + (s >> 1) * 32 + (s & 1) * 8, tc::mnmajor_desc(kq, kKQBlock, s),
                            kIdDS, s > 0);
+          if (!kDsSingle) {
 #pragma unroll
-          for (int s = 0; s < 4; ++s)
-            tc::mma_tmem_a(tmem + kTmDS, tmu + (s >> 1) * 32 + 16 + (s & 1) * 8,
-                           tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, true);
+            for (int s = 0; s < 4; ++s)
+              tc::mma_tmem_a(tmem + kTmDS, tmu + (s >> 1) * 32 + 16 + (s & 1) * 8,
+                             tc::mnmajor_desc(kq, kKQBlock, s), kIdDS, true);
+          }
           tc::commit(&bars[kBarS2]);
 #pragma unroll
           for (int s = 0; s < 4; ++s)
