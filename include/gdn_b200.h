@@ -248,6 +248,8 @@ size_t gdn_prefill_workspace_size(const gdn_prefill_args_t* args);
  * describes it: analysis/wave15-attention-research/MECHANISMS.md:398-445); its
  * results are defined by T applications of the reference decode recurrence
  * (analysis/wave15-attention-architecture/reference/pytorch_reference_gdn.py:38-91).
+ * The state update takes the per-token residuals beta (v - k^T S) as f16, so
+ * their magnitude must stay below 65,504 (|v| up to about 1e4).
  */
 int gdn_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
@@ -294,7 +296,8 @@ int gdn_prefill_launch_noalloc(const gdn_prefill_args_t* args, gdn_stream_t stre
  *   - NULL: the recurrent form (state on chip, CUDA cores), any listed d.
  *   - non-NULL (d_k = d_v = 128 only; >= kda_prefill_workspace_size bytes,
  *     16-byte aligned, as are the states): the chunked tensor-core form,
- *     64-token chunks, the per-channel decays inside the WY transform.
+ *     64-token chunks, the per-channel decays inside the WY transform; the
+ *     same f16 range condition on the residuals as gdn_prefill_launch.
  */
 int kda_prefill_launch(const gdn_prefill_args_t* args, gdn_stream_t stream);
 
