@@ -307,6 +307,11 @@ def _workspace(dev, need: int, given):
     """The caller's workspace tensor, or a per-device cached one of at least
     ``need`` bytes (grown when a larger problem comes)."""
     if given is not None:
+        if given.device != dev or not given.is_contiguous():
+            raise GDNError(f"workspace must be a contiguous tensor on {dev}", 2)
+        if given.numel() * given.element_size() < need:
+            raise GDNError(f"workspace holds {given.numel() * given.element_size()} bytes; "
+                           f"these shapes need {need}", 7)
         return given
     ws = _workspaces.get(dev.index)
     if ws is None or ws.numel() < need:

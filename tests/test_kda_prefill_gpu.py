@@ -162,3 +162,14 @@ def test_kda_chunked_rejects_other_head_dims(pkg, inputs):
     p = inputs.make_kda_prefill_inputs(1, 16, 1, 1, 64, seed=0)
     with pytest.raises(pkg.GDNError):
         pkg.kda_prefill(*_dev(p), form="chunked")
+
+
+def test_kda_chunked_rejects_small_or_foreign_workspace(pkg, inputs):
+    """A caller-supplied workspace must be on the inputs' device and large
+    enough; both are refused before any launch."""
+    p = inputs.make_kda_prefill_inputs(1, 128, 1, 1, 128, seed=0)
+    x = _dev(p)
+    with pytest.raises(pkg.GDNError):
+        pkg.kda_prefill(*x, form="chunked", workspace=torch.empty(1024, dtype=torch.uint8, device=DEV))
+    with pytest.raises(pkg.GDNError):
+        pkg.kda_prefill(*x, form="chunked", workspace=torch.empty(1 << 20, dtype=torch.uint8))
