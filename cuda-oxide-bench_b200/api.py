@@ -305,7 +305,10 @@ _workspaces: dict[int, torch.Tensor] = {}
 
 def _workspace(dev, need: int, given):
     """The caller's workspace tensor, or a per-device cached one of at least
-    ``need`` bytes (grown when a larger problem comes)."""
+    ``need`` bytes (grown when a larger problem comes).  The cached one is
+    shared by every gdn_prefill / kda_prefill call on the device, so calls
+    whose kernels may overlap on the GPU (different streams or threads) must
+    each pass their own ``workspace``."""
     if given is not None:
         if given.device != dev or not given.is_contiguous():
             raise GDNError(f"workspace must be a contiguous tensor on {dev}", 2)
